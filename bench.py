@@ -1,0 +1,417 @@
+"""Benchmark of the myvllm attention hot path on B200.
+
+Default (the headline line): config 1 -- one Gated-DeltaNet prefill layer, i.e.
+causal_conv1d_fn over 8192 qkv channels -> l2norm(q, k) -> chunk_gated_delta_rule
+(chunk 64), 8 sequences with lengths ~U[512, 8192], bf16 activations, fp32 state.
+Metric: prefill tokens/s.  Multi-GPU (torchrun): every rank runs its own independent
+config-1 batch (sequences are independent objects; no collective on the data path),
+so scaling is weak and ``value`` = all ranks' tokens / max-over-ranks step time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
+                    [--config c1|c2|c3]
+
+``--impl reference`` times the CPU restatement of the reference path (the oracle; the
+reference's own kernels are Triton and do not run on a CPU) on the host's cores.
+``--config c2|c3`` prints the same kind of line for the decode / full-attention
+configs (diagnostic; the headline is c1).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def profiled_traffic(kernel_key: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(kernel_key)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._proc = None
+
+    def __enter__(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self._proc = None
+        return self
+
+    def _read(self):
+        for line in self._proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 6:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        mhz = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[2 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- c1 ----
+def c1_step(inp, ops, events=None):
+    """conv1d -> l2norm(q,k) -> chunked GDN; returns o.  ``events`` brackets the GDN launch."""
+    from myvllm_b200 import workloads as W
+
+    qkv = ops.causal_conv1d_fn(inp["x"], inp["conv_w"], inp["conv_state"], inp["idx"], inp["cu"])
+    q, k, v = W.split_qkv(qkv)
+    q, k = W.l2norm(q), W.l2norm(k)
+    if events is not None:
+        events[0].record()
+    o = ops.chunk_gated_delta_rule(q, k, v, inp["g"], inp["beta"], inp["state"], inp["idx"], inp["cu"])
+    if events is not None:
+        events[1].record()
+    return o
+
+
+class _C1Ops:
+    def __init__(self):
+        from myvllm_b200.ops.causal_conv1d import causal_conv1d_fn
+        from myvllm_b200.ops.gated_delta_rule.gated_delta_rule import chunk_gated_delta_rule
+
+        self.causal_conv1d_fn = causal_conv1d_fn
+        self.chunk_gated_delta_rule = chunk_gated_delta_rule
+
+
+def cpu_baseline_c1(budget_s: float = 12.0, seed: int = 0):
+    """The oracle (numpy restatement of the reference path) on a bounded sample of the
+    config-1 workload: whole sequences of the seeded batch, conv1d + l2norm + chunked
+    GDN, all 32 heads, until ``budget_s`` of CPU time is spent.  Returns tokens/s."""
+    import oracle
+    from myvllm_b200 import workloads as W
+
+    lengths = W.seq_lengths(8, 512, 8192, seed)
+    rng = np.random.default_rng(seed)
+    tokens, spent = 0, 0.0
+    for L in lengths:
+        x = rng.standard_normal((L, W.GDN_CH)).astype(np.float32)
+        w = (0.02 * rng.standard_normal((W.GDN_CH, W.GDN_W))).astype(np.float32)
+        cst = np.zeros((1, W.GDN_W - 1, W.GDN_CH), np.float32)
+        g = -rng.uniform(0.01, 1.0, (L, W.GDN_HV)).astype(np.float32)
+        beta = rng.uniform(0, 1, (L, W.GDN_HV)).astype(np.float32)
+        st = np.zeros((1, W.GDN_HV, W.GDN_DK, W.GDN_DV), np.float32)
+        t0 = time.perf_counter()
+        qkv = oracle.conv.conv1d_fn(x, w, cst, np.array([0]), np.array([0, L]), dtype=np.float32)
+        q = qkv[:, :2048].reshape(L, 16, 128)
+        k = qkv[:, 2048:4096].reshape(L, 16, 128)
+        v = qkv[:, 4096:].reshape(L, 32, 128)
+        q = q / np.sqrt((q * q).sum(-1, keepdims=True) + 1e-6)
+        k = k / np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+        oracle.gdn.chunked(q, k, v, g, beta, st, np.array([0]), np.array([0, L]), 64, dtype=np.float32)
+        spent += time.perf_counter() - t0
+        tokens += L
+        if spent >= budget_s:
+            break
+    return tokens / spent, tokens, spent
+
+
+def run_c1(args, rank, world, device):
+    from myvllm_b200 import workloads as W
+    from myvllm_b200.ops.gated_delta_rule.gated_delta_rule import chunk_gated_delta_rule  # noqa: F401
+    import oracle
+
+    ops = _C1Ops()
+    inp = W.c1_inputs(device, seed=rank)
+    T = inp["T"]
+    for _ in range(args.warmup):
+        c1_step(inp, ops)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index or 0) as clk:
+        start.record()
+        for i in range(args.steps):
+            c1_step(inp, ops, ev[i])
+        stop.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    gdn_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        t = torch.tensor([ms, float(T)], device=device, dtype=torch.float64)
+        mx = t.clone()
+        torch.distributed.all_reduce(mx[:1], op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(t[1:], op=torch.distributed.ReduceOp.SUM)
+        ms, tokens_all = mx[0].item(), t[1].item()
+        torch.distributed.barrier()
+    else:
+        tokens_all = float(T)
+
+    # end to end through the public op API with host buffers: H2D of the step's inputs
+    # from pinned memory, the step, D2H of the output
+    host = {k: inp[k].cpu().pin_memory() for k in ("x", "g", "beta", "cu")}
+    o_host = torch.empty((T, W.GDN_HV, W.GDN_DV), dtype=torch.bfloat16).pin_memory()
+    dev_in = dict(inp)
+    for _ in range(2):
+        for k_ in host:
+            dev_in[k_].copy_(host[k_], non_blocking=True)
+        o_host.copy_(c1_step(dev_in, ops), non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 2)
+    e0.record()
+    for _ in range(e2e_steps):
+        for k_ in host:
+            dev_in[k_].copy_(host[k_], non_blocking=True)
+        o_host.copy_(c1_step(dev_in, ops), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = t.item()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = o_host.numel() * o_host.element_size()
+
+    if rank != 0:
+        return None
+    pk, src = peaks()
+    flops = T * W.GDN_HV * oracle.gdn.flops_per_token_per_head(64, W.GDN_DK, W.GDN_DV)
+    achieved = flops / (gdn_ms * 1e-3) / 1e12
+    traffic = profiled_traffic("gdn_chunk_c1")
+    base_tps, base_tok, base_s = cpu_baseline_c1()
+    line = {
+        "metric": "prefill tokens/s (GDN layer: conv1d + chunked gated delta rule)",
+        "value": tokens_all / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "c1: GDN prefill layer, 8 seqs ~U[512,8192] (seed 0+rank), 16/32 heads x 128, "
+                               "conv W=4 over 8192 ch, chunk 64",
+                   "tokens_per_rank": T, "lengths_rank0": inp["lengths"], "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2 (x is %.0f MB)" % (inp["x"].numel() * 2 / 1e6)},
+        "roofline": {"bound": "tensor", "kernel": "gdn_chunk_kernel", "achieved": achieved,
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
+                     "peak_source": f"{src} bf16 burst", "flops_per_launch": flops, "launch_ms": gdn_ms,
+                     "traffic": traffic},
+        "cpu_baseline": {"value": base_tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{base_tok} tokens of config-1 sequences (numpy oracle, fp32), {base_s:.1f} s"},
+        "e2e": {"value": tokens_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    return line
+
+
+# ----------------------------------------------------------------------------- c2 ----
+def run_c2(args, rank, world, device):
+    from myvllm_b200 import workloads as W
+    from myvllm_b200.ops.causal_conv1d import causal_conv1d_update
+    from myvllm_b200.ops.gated_delta_rule.fused_recurrent_gdn import fused_recurrent_gdn
+
+    inp = W.c2_inputs(device, seed=rank)
+
+    def step(ev=None):
+        qkv = causal_conv1d_update(inp["x"], inp["conv_w"], inp["conv_state"], inp["idx"])
+        q, k, v = W.split_qkv(qkv)
+        q, k = W.l2norm(q), W.l2norm(k)
+        if ev:
+            ev[0].record()
+        o = fused_recurrent_gdn(q, k, v, inp["g"], inp["beta"], inp["state"], inp["idx"])
+        if ev:
+            ev[1].record()
+        return o
+
+    for _ in range(args.warmup):
+        step()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index or 0) as clk:
+        s0.record()
+        for i in range(args.steps):
+            step(evs[i])
+        s1.record()
+        torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / args.steps
+    rec_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    state_bytes = 2 * inp["state"].numel() * 4
+    pk, src = peaks()
+    gbs = state_bytes / (rec_ms * 1e-3) / 1e9
+    return {"metric": "decode us/step (GDN layer: conv1d update + recurrent GDN)", "value": ms * 1e3, "unit": "us",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "c2: 256 seqs, state [256,32,128,128] fp32"},
+            "roofline": {"bound": "hbm", "kernel": "gdn_recurrent_kernel", "achieved": gbs, "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": src, "launch_us": rec_ms * 1e3,
+                         "traffic": profiled_traffic("gdn_recurrent_c2")},
+            "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
+
+
+# ----------------------------------------------------------------------------- c3 ----
+def run_c3(args, rank, world, device):
+    import oracle
+    from myvllm_b200 import workloads as W
+    from myvllm_b200.ops.full_attention import flash_attention_prefill
+    from myvllm_b200.ops.kv_cache import store_kvcache
+
+    inp = W.c3_inputs(device, seed=rank)
+    kc = torch.zeros(inp["n_blocks"], inp["block_size"], 2, 256, dtype=torch.bfloat16, device=device)
+    vc = torch.zeros_like(kc)
+
+    def step(ev=None):
+        store_kvcache(inp["k"], inp["v"], kc, vc, inp["slot_mapping"])
+        if ev:
+            ev[0].record()
+        o = flash_attention_prefill(inp["q"], inp["k"], inp["v"], inp["cu"], inp["scale"], 16, 2, 256, 256, True)
+        if ev:
+            ev[1].record()
+        return o
+
+    for _ in range(args.warmup):
+        step()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index or 0) as clk:
+        s0.record()
+        for i in range(args.steps):
+            step(evs[i])
+        s1.record()
+        torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / args.steps
+    fa_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    flops = oracle.attention.varlen_flops(inp["cu"].cpu().numpy(), 16, 256, 256, True)
+    pk, src = peaks()
+    tf = flops / (fa_ms * 1e-3) / 1e12
+    return {"metric": "prefill tokens/s (full attention: KV write + varlen causal FA)",
+            "value": inp["T"] / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "c3: Hq16/Hkv2/D256 causal, 8 seqs ~U[1024,16384]", "tokens": inp["T"]},
+            "roofline": {"bound": "tensor", "kernel": "flash_prefill_kernel", "achieved": tf,
+                         "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": tf / pk["bf16_tflops"],
+                         "peak_source": src, "launch_ms": fa_ms, "flops_per_launch": flops,
+                         "traffic": profiled_traffic("flash_prefill_c3")},
+            "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
+
+
+# ------------------------------------------------------------------------ reference ----
+def run_reference(args):
+    """The CPU restatement of the reference path on this host's cores, on the c1 metric."""
+    base = []
+    for _ in range(args.warmup):
+        pass  # the oracle has no warm-up state
+    t_all = 0.0
+    tok_all = 0
+    for i in range(args.steps):
+        tps, tok, s = cpu_baseline_c1(budget_s=max(2.0, 30.0 / max(1, args.steps)), seed=0)
+        base.append(tps)
+        t_all += s
+        tok_all += tok
+    v = tok_all / t_all
+    return {"metric": "prefill tokens/s (GDN layer: conv1d + chunked gated delta rule)", "value": v,
+            "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * t_all / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "c1: GDN prefill layer, 8 seqs ~U[512,8192] (seed 0), bounded sample per step"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{tok_all} tokens over {args.steps} steps (numpy oracle of the reference "
+                                       "path; its Triton kernels do not run on a CPU)"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3"])
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    from myvllm_b200 import _lib
+
+    _lib.load()  # fail loudly if the library is missing
+    fn = {"c1": run_c1, "c2": run_c2, "c3": run_c3}[args.config]
+    line = fn(args, rank, world, device)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

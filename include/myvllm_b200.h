@@ -1,0 +1,142 @@
+/*
+ * myvllm_b200 -- C ABI of the B200 (sm_100a) attention hot-path kernels.
+ *
+ * One entry point per reference op.  Every entry point takes plain tensor
+ * descriptors (device pointer + dtype + shape + strides in elements), enqueues its
+ * kernels on the given CUDA stream (`void*` = cudaStream_t, NULL = legacy default
+ * stream) and returns a status code.  Nothing here allocates device memory or
+ * synchronises the host; callers own every buffer (outputs, states, workspaces).
+ *
+ * Reference interfaces replaced (paths relative to the reference project, `m/` =
+ * `src/myvllm/`):
+ *   mvb_causal_conv1d_fn        m/ops/causal_conv1d.py:221-273       causal_conv1d_fn
+ *   mvb_causal_conv1d_update    m/ops/causal_conv1d.py:434-470       causal_conv1d_update
+ *   mvb_chunk_gated_delta_rule  m/ops/gated_delta_rule/gated_delta_rule.py:31-66
+ *   mvb_fused_recurrent_gdn     m/ops/gated_delta_rule/fused_recurrent_gdn.py:105-166
+ *                               (also recurrent_gated_delta_rule, gated_delta_rule.py:69-92)
+ *   mvb_flash_attention_prefill m/ops/full_attention.py:114-173      flash_attention_prefill
+ *   mvb_paged_attention_decode  m/ops/full_attention.py:282-335      paged_flash_attention_decode
+ *   mvb_paged_attention_prefill m/ops/full_attention.py:454-512      paged_flash_attention_prefill
+ *   mvb_store_kvcache           (no kernel in the reference; layout from m/ops/full_attention.py:186-195,
+ *                                slot_mapping convention from m/utils/context.py:15)
+ *   mvb_rmsnorm_gated           m/layers/norm.py:44-58                RMSNormGated.forward
+ *
+ * Conventions kept from the reference:
+ *   - index tensors (cu_seqlens, *_indices, block_tables, context_lens, slot_mapping) are int32;
+ *   - cu_seqlens[0] = 0, cu_seqlens[n_seqs] = total tokens;
+ *   - conv_state [S_max, W-1, dim], recurrent_state [S_max, Hv, K, V] (fp32), mutated in
+ *     place at the rows named by the index tensors;
+ *   - paged caches [n_blocks, block_size, Hkv, D]; slot = block * block_size + offset, -1 = skip;
+ *   - v-head h uses k-head h / (Hv / Hk); q-head h uses kv-head h / (Hq / Hkv).
+ */
+#ifndef MYVLLM_B200_H_
+#define MYVLLM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define MVB_OK 0
+#define MVB_ERR_ARG 1          /* malformed argument: shape/dtype/stride mismatch, null pointer */
+#define MVB_ERR_UNSUPPORTED 2  /* well-formed but outside what the kernels implement */
+#define MVB_ERR_CUDA 3         /* a CUDA runtime call or kernel launch failed */
+
+/* dtypes */
+#define MVB_F32 0
+#define MVB_BF16 1
+#define MVB_F16 2
+#define MVB_I32 3
+
+#define MVB_MAX_DIMS 6
+
+typedef struct mvb_tensor {
+  void* data;                     /* device pointer; may be NULL only if some dim is 0 */
+  int32_t dtype;                  /* MVB_F32 / MVB_BF16 / MVB_F16 / MVB_I32 */
+  int32_t ndim;
+  int64_t shape[MVB_MAX_DIMS];
+  int64_t stride[MVB_MAX_DIMS];   /* in elements */
+} mvb_tensor;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mvb_version(void);
+
+/* Message for the last non-zero status returned on the calling host thread. */
+const char* mvb_last_error(void);
+
+/* Varlen causal depthwise conv (width W <= 8) + SiLU over packed sequences.
+ * x [T, dim]; weight [dim, W]; conv_state [S_max, W-1, dim] (read as history, then
+ * overwritten with the last W-1 inputs of each sequence); conv_state_indices [S];
+ * cu_seqlens [S+1]; out [T, dim] (same dtype as x).  activation: 1 = SiLU, 0 = none. */
+int mvb_causal_conv1d_fn(const mvb_tensor* x, const mvb_tensor* weight, mvb_tensor* conv_state,
+                         const mvb_tensor* conv_state_indices, const mvb_tensor* cu_seqlens,
+                         mvb_tensor* out, int activation, void* stream);
+
+/* One token per sequence: x [S, dim]; shifts conv_state[idx] in place; out [S, dim]. */
+int mvb_causal_conv1d_update(const mvb_tensor* x, const mvb_tensor* weight, mvb_tensor* conv_state,
+                             const mvb_tensor* conv_state_indices, mvb_tensor* out, int activation,
+                             void* stream);
+
+/* Chunked gated delta rule (prefill).  q,k [T, Hk, K]; v [T, Hv, V]; g, beta [T, Hv]
+ * (g = natural-log decay); recurrent_state [S_max, Hv, K, V] fp32 -- the rows
+ * recurrent_state_indices[s] are read as the initial state and overwritten with the
+ * final state; cu_seqlens [S+1]; o [T, Hv, V] (dtype of v).  scale <= 0 means K^-0.5. */
+int mvb_chunk_gated_delta_rule(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
+                               const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,
+                               const mvb_tensor* recurrent_state_indices, const mvb_tensor* cu_seqlens,
+                               mvb_tensor* o, float scale, void* stream);
+
+/* Recurrent gated delta rule, one token per sequence (decode).  q,k [S, Hk, K];
+ * v [S, Hv, V]; g, beta [S, Hv]; state [S_max, Hv, K, V] fp32 updated in place;
+ * o [S, Hv, V].  scale <= 0 means K^-0.5. */
+int mvb_fused_recurrent_gdn(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
+                            const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,
+                            const mvb_tensor* recurrent_state_indices, mvb_tensor* o, float scale,
+                            void* stream);
+
+/* Varlen (optionally causal) attention.  q [T, Hq, D]; k [T, Hkv, D]; v [T, Hkv, Dv];
+ * cu_seqlens [S+1]; o [T, Hq, Dv] (dtype of q).  bf16/f16 only. */
+int mvb_flash_attention_prefill(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
+                                const mvb_tensor* cu_seqlens, float scale, int num_heads, int num_kv_heads,
+                                int head_dim, int head_v_dim, int is_causal, mvb_tensor* o, void* stream);
+
+/* Bytes of workspace mvb_paged_attention_decode needs for this problem size. */
+size_t mvb_paged_attention_decode_workspace_size(int64_t n_seqs, int64_t num_kv_heads, int64_t head_v_dim,
+                                                 int64_t max_context_len);
+
+/* One query per sequence over a paged KV cache.  q [S, Hq, D]; k_cache [NB, bs, Hkv, D];
+ * v_cache [NB, bs, Hkv, Dv]; block_tables [S, max_blocks]; context_lens [S];
+ * o [S, Hq, Dv].  workspace: at least mvb_paged_attention_decode_workspace_size(...)
+ * bytes of device memory (split-KV partial results), or NULL/0 to run unsplit.
+ * max_context_len: an upper bound on context_lens (<= max_blocks * block_size). */
+int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor* k_cache, const mvb_tensor* v_cache,
+                               const mvb_tensor* block_tables, const mvb_tensor* context_lens, float scale,
+                               int block_size, int64_t max_context_len, mvb_tensor* o, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Prefill continuing from a paged cache: the L_s queries of sequence s sit at positions
+ * context_lens[s] - L_s + i and attend causally to cached tokens [0, context_lens[s]).
+ * q [T, Hq, D]; cu_seqlens [S+1]; other arguments as in mvb_paged_attention_decode. */
+int mvb_paged_attention_prefill(const mvb_tensor* q, const mvb_tensor* k_cache, const mvb_tensor* v_cache,
+                                const mvb_tensor* block_tables, const mvb_tensor* context_lens,
+                                const mvb_tensor* cu_seqlens, float scale, int block_size, mvb_tensor* o,
+                                void* stream);
+
+/* Scatter k [T, Hkv, D], v [T, Hkv, Dv] into k_cache/v_cache [NB, bs, Hkv, D*] at
+ * slot_mapping[t] (int32; -1 = skip). */
+int mvb_store_kvcache(const mvb_tensor* k, const mvb_tensor* v, mvb_tensor* k_cache, mvb_tensor* v_cache,
+                      const mvb_tensor* slot_mapping, void* stream);
+
+/* out = x * rsqrt(mean(x^2) + eps) * weight * silu(gate), per row of the last dim.
+ * x, gate, out [N, D]; weight [D]. */
+int mvb_rmsnorm_gated(const mvb_tensor* x, const mvb_tensor* gate, const mvb_tensor* weight, float eps,
+                      mvb_tensor* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MYVLLM_B200_H_ */

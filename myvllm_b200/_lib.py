@@ -1,0 +1,136 @@
+"""ctypes binding of ``libmyvllm_b200.so`` (declared in ``include/myvllm_b200.h``).
+
+The library is the only compute path: there is no CPU or eager-PyTorch fallback.
+If the shared object is missing, importing an op raises immediately; if a kernel
+rejects its arguments, the op raises ``RuntimeError`` naming the op and the reason.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("MYVLLM_B200_LIB", os.path.join(_HERE, "_lib", "libmyvllm_b200.so"))
+
+MAX_DIMS = 6
+MVB_F32, MVB_BF16, MVB_F16, MVB_I32 = 0, 1, 2, 3
+_DTYPES = {torch.float32: MVB_F32, torch.bfloat16: MVB_BF16, torch.float16: MVB_F16, torch.int32: MVB_I32}
+_STATUS = {1: "bad argument", 2: "unsupported", 3: "CUDA error"}
+
+
+class MvbTensor(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("dtype", ctypes.c_int32),
+        ("ndim", ctypes.c_int32),
+        ("shape", ctypes.c_int64 * MAX_DIMS),
+        ("stride", ctypes.c_int64 * MAX_DIMS),
+    ]
+
+
+_T = ctypes.POINTER(MvbTensor)
+_P = ctypes.c_void_p
+
+# name -> (restype, argtypes); mirrors include/myvllm_b200.h
+SIGNATURES = {
+    "mvb_version": (ctypes.c_int, []),
+    "mvb_last_error": (ctypes.c_char_p, []),
+    "mvb_causal_conv1d_fn": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, ctypes.c_int, _P]),
+    "mvb_causal_conv1d_update": (ctypes.c_int, [_T, _T, _T, _T, _T, ctypes.c_int, _P]),
+    "mvb_chunk_gated_delta_rule": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, _T, _T, _T, ctypes.c_float, _P]),
+    "mvb_fused_recurrent_gdn": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, _T, _T, ctypes.c_float, _P]),
+    "mvb_flash_attention_prefill": (ctypes.c_int, [_T, _T, _T, _T, ctypes.c_float, ctypes.c_int, ctypes.c_int,
+                                                   ctypes.c_int, ctypes.c_int, ctypes.c_int, _T, _P]),
+    "mvb_paged_attention_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int64] * 4),
+    "mvb_paged_attention_decode": (ctypes.c_int, [_T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int, ctypes.c_int64,
+                                                  _T, _P, ctypes.c_size_t, _P]),
+    "mvb_paged_attention_prefill": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int, _T, _P]),
+    "mvb_store_kvcache": (ctypes.c_int, [_T, _T, _T, _T, _T, _P]),
+    "mvb_rmsnorm_gated": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, _T, _P]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(
+                    f"myvllm_b200: {LIB_PATH} is missing; build it with `python -m myvllm_b200.build` "
+                    "(there is no fallback implementation)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def desc(t: torch.Tensor) -> MvbTensor:
+    """Descriptor of a device tensor (shape/strides in elements)."""
+    if t.dim() > MAX_DIMS:
+        raise ValueError(f"myvllm_b200: tensors of rank > {MAX_DIMS} are not supported")
+    d = MvbTensor()
+    d.data = t.data_ptr() if t.numel() > 0 else None
+    try:
+        d.dtype = _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"myvllm_b200: unsupported dtype {t.dtype}") from None
+    d.ndim = t.dim()
+    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
+        d.shape[i] = s
+        d.stride[i] = st
+    return d
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(op: str, *tensors: torch.Tensor) -> None:
+    dev = None
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(f"{op}: all tensors must be CUDA tensors (this library has no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{op}: tensors are on different devices ({dev} vs {t.device})")
+
+
+def check(op: str, status: int) -> None:
+    if status != 0:
+        msg = load().mvb_last_error().decode(errors="replace")
+        raise RuntimeError(f"{op}: {_STATUS.get(status, status)}: {msg}")
+
+
+def call(op: str, fn_name: str, *args) -> None:
+    """Calls an int-returning entry point and raises on a non-zero status."""
+    lib = load()
+    wrapped = [ctypes.byref(a) if isinstance(a, MvbTensor) else a for a in args]
+    check(op, getattr(lib, fn_name)(*wrapped))
+
+
+_workspaces: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A per-device scratch buffer, grown on demand and reused across calls on the
+    current stream (kernels on one stream are ordered, so reuse is safe there)."""
+    key = (device.type, device.index)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf

@@ -1,0 +1,38 @@
+// Status plumbing shared by every entry point of libmyvllm_b200.
+#include "common.cuh"
+
+namespace mvb {
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int check_tensor(const mvb_tensor* t, const char* op, const char* name, int ndim) {
+  if (t == nullptr) MVB_FAIL(MVB_ERR_ARG, "%s: %s is NULL", op, name);
+  if (t->ndim != ndim) MVB_FAIL(MVB_ERR_ARG, "%s: %s must have %d dims, got %d", op, name, ndim, t->ndim);
+  for (int i = 0; i < ndim; ++i)
+    if (t->shape[i] < 0) MVB_FAIL(MVB_ERR_ARG, "%s: %s has a negative extent", op, name);
+  if (numel(t) > 0 && t->data == nullptr) MVB_FAIL(MVB_ERR_ARG, "%s: %s has no data pointer", op, name);
+  return MVB_OK;
+}
+
+int num_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+}  // namespace mvb
+
+extern "C" {
+
+int mvb_version(void) { return 100; }
+
+const char* mvb_last_error(void) { return mvb::g_last_error; }
+
+}  // extern "C"

@@ -1,0 +1,418 @@
+// Paged-KV decode attention (one query per sequence), HBM-bound.
+//
+// Replaces _paged_flash_attention_decode_kernel (m/ops/full_attention.py:176-279), which
+// runs one program per (seq, q-head) and so streams every KV page once per q-head
+// (8x for GQA 8:1).  Here one CTA owns (split, kv-head, seq) and computes all G =
+// Hq / Hkv query heads of that kv-head together, so each cached K/V row crosses HBM
+// once:
+//   S[g, t] = scale q_g . k_t ;  online softmax over t (exp2, fp32) ;  O[g] = sum p v_t
+// Tiles of 64 tokens are gathered through the block table with 16-byte cp.async into
+// an XOR-swizzled, double-buffered shared-memory ring; each of the 4 warps takes 16
+// tokens of a tile and runs QK^T and PV on mma.sync m16n8k16 (G padded to 16 rows;
+// the padded rows are never written).  Long contexts are split across CTAs
+// (flash-decoding); split results (normalised O and log2-sum-exp) go to the caller's
+// workspace and a second kernel merges them.
+#include "common.cuh"
+
+namespace mvb {
+
+struct DecodeParams {
+  const void* q;
+  const void *kc, *vc;
+  const int32_t* bt;
+  const int32_t* ctx;
+  void* o;
+  float* part_o;     // [S, Hkv, n_splits, 16, Dv] fp32, or null when n_splits == 1
+  float* part_lse;   // [S, Hkv, n_splits, 16]
+  int64_t sq_s, sq_h, so_s, so_h;
+  int64_t skc_b, skc_t, skc_h, svc_b, svc_t, svc_h;
+  int64_t sbt_s, sbt_b;
+  int hq, hkv, group, block_size, max_blocks, n_splits, split_len;
+  float scale_log2;  // scale * log2(e)
+};
+
+namespace {
+
+constexpr int kTile = 64;
+constexpr int kWarps = 4;
+
+template <int D>
+struct DecodeSmem {
+  static constexpr int kRowBytes = D * 2;
+  static constexpr int kTileBytes = kTile * kRowBytes;
+  static constexpr int kStageBytes = 2 * kTileBytes;  // K + V
+  static constexpr int kQBytes = 16 * kRowBytes;
+  static constexpr int kBytes = 2 * kStageBytes + kQBytes;
+};
+
+// Byte offset of 16-byte chunk `c` of row `r` in a swizzled [rows][D] bf16 tile.
+template <int D>
+__device__ __forceinline__ int swz(int r, int c) {
+  return r * (D * 2) + ((c ^ (r & 7)) << 4);
+}
+
+template <typename T, int D>
+__device__ __forceinline__ void load_tile(const DecodeParams& p, char* sK, char* sV, int seq, int kvh, int t0,
+                                          int ctx) {
+  constexpr int CH = D / 8;  // 16-byte chunks per row
+  const char* kc = static_cast<const char*>(p.kc);
+  const char* vc = static_cast<const char*>(p.vc);
+  for (int i = threadIdx.x; i < kTile * CH; i += kWarps * 32) {
+    const int r = i / CH, c = i % CH;
+    const int t = t0 + r;
+    const bool ok = t < ctx;
+    int64_t koff = 0, voff = 0;
+    if (ok) {
+      const int blk = p.bt[seq * p.sbt_s + (t / p.block_size) * p.sbt_b];
+      const int off = t % p.block_size;
+      koff = (blk * p.skc_b + off * p.skc_t + kvh * p.skc_h) * 2 + c * 16;
+      voff = (blk * p.svc_b + off * p.svc_t + kvh * p.svc_h) * 2 + c * 16;
+    }
+    cp_async16(sK + swz<D>(r, c), kc + koff, ok);
+    cp_async16(sV + swz<D>(r, c), vc + voff, ok);
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams p) {
+  using SM = DecodeSmem<D>;
+  extern __shared__ __align__(128) char smem[];
+  char* sQ = smem + 2 * SM::kStageBytes;
+  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ctx = p.ctx[seq];
+  const int t_begin = split * p.split_len;
+  const int t_end = min(ctx, t_begin + p.split_len);
+  const int G = p.group;
+
+  if (t_begin >= t_end) {
+    if (p.n_splits > 1 && tid < 16) {
+      const int64_t pi = ((int64_t)seq * p.hkv + kvh) * p.n_splits + split;
+      p.part_lse[pi * 16 + tid] = -INFINITY;
+    } else if (p.n_splits == 1) {  // empty context: zeros
+      T* o = static_cast<T*>(p.o);
+      for (int i = tid; i < G * D; i += kWarps * 32)
+        o[seq * p.so_s + (kvh * G + i / D) * p.so_h + i % D] = from_f32<T>(0.f);
+    }
+    return;
+  }
+
+  // Q -> smem (rows >= G zero).
+  {
+    const T* q = static_cast<const T*>(p.q);
+    constexpr int CH = D / 8;
+    for (int i = tid; i < 16 * CH; i += kWarps * 32) {
+      const int r = i / CH, c = i % CH;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (r < G) val = *reinterpret_cast<const uint4*>(q + seq * p.sq_s + (kvh * G + r) * p.sq_h + c * 8);
+      *reinterpret_cast<uint4*>(sQ + swz<D>(r, c)) = val;
+    }
+  }
+
+  const int n_tiles = (t_end - t_begin + kTile - 1) / kTile;
+  load_tile<T, D>(p, smem, smem + SM::kTileBytes, seq, kvh, t_begin, t_end);
+  cp_async_commit();
+
+  float acc[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows lane/4 and lane/4 + 8
+
+  for (int it = 0; it < n_tiles; ++it) {
+    const int stage = it & 1;
+    if (it + 1 < n_tiles) {
+      char* nb = smem + (stage ^ 1) * SM::kStageBytes;
+      load_tile<T, D>(p, nb, nb + SM::kTileBytes, seq, kvh, t_begin + (it + 1) * kTile, t_end);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const char* sK = smem + stage * SM::kStageBytes;
+    const char* sV = sK + SM::kTileBytes;
+
+    // S = Q K^T for this warp's 16 tokens (two n8 fragments).
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4], b[4];
+      {
+        const int r = lane & 15, c = kk * 2 + (lane >> 4);
+        ldmatrix_x4(a[0], a[1], a[2], a[3], smem_u32(sQ + swz<D>(r, c)));
+      }
+      {
+        // matrices: (tokens 0-7, k lo), (tokens 0-7, k hi), (tokens 8-15, k lo), (tokens 8-15, k hi)
+        const int r = warp * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int c = kk * 2 + ((lane >> 3) & 1);
+        ldmatrix_x4(b[0], b[1], b[2], b[3], smem_u32(sK + swz<D>(r, c)));
+      }
+      mma16816<T>(s[0], a, b);
+      mma16816<T>(s[1], a, b + 2);
+    }
+    // mask tokens past the end, scale into log2 domain
+    const int tbase = t_begin + it * kTile + warp * 16 + (lane & 3) * 2;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = tbase + n * 8 + (j & 1);
+        s[n][j] = t < t_end ? s[n][j] * p.scale_log2 : -INFINITY;
+      }
+    float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+    float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+    // a warp whose 16 tokens are all masked keeps m = -inf: guard the rescale
+    const float a0 = nm0 == -INFINITY ? 1.f : exp2f(m0 - nm0);
+    const float a1 = nm1 == -INFINITY ? 1.f : exp2f(m1 - nm1);
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      s[n][0] = nm0 == -INFINITY ? 0.f : exp2f(s[n][0] - nm0);
+      s[n][1] = nm0 == -INFINITY ? 0.f : exp2f(s[n][1] - nm0);
+      s[n][2] = nm1 == -INFINITY ? 0.f : exp2f(s[n][2] - nm1);
+      s[n][3] = nm1 == -INFINITY ? 0.f : exp2f(s[n][3] - nm1);
+      ps0 += s[n][0] + s[n][1];
+      ps1 += s[n][2] + s[n][3];
+    }
+    l0 = l0 * a0 + ps0;
+    l1 = l1 * a1 + ps1;
+    m0 = nm0;
+    m1 = nm1;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      acc[i][0] *= a0; acc[i][1] *= a0; acc[i][2] *= a1; acc[i][3] *= a1;
+    }
+    // P as the A operand (16 x 16 tokens) of PV.
+    uint32_t pa[4];
+    pa[0] = pack2<T>(s[0][0], s[0][1]);
+    pa[1] = pack2<T>(s[0][2], s[0][3]);
+    pa[2] = pack2<T>(s[1][0], s[1][1]);
+    pa[3] = pack2<T>(s[1][2], s[1][3]);
+#pragma unroll
+    for (int nn = 0; nn < D / 16; ++nn) {
+      uint32_t b[4];
+      // V rows = tokens (k), 16 columns (two n8 fragments), transposed load.
+      const int r = warp * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int c = nn * 2 + (lane >> 4);
+      ldmatrix_x4_trans(b[0], b[1], b[2], b[3], smem_u32(sV + swz<D>(r, c)));
+      mma16816<T>(acc[nn * 2], pa, b);
+      mma16816<T>(acc[nn * 2 + 1], pa, b + 2);
+    }
+    __syncthreads();  // stage is free for the next prefetch
+  }
+  cp_async_wait<0>();
+
+  // Row sums across the 4 lanes of a quad.
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  // Merge the 4 warps through shared memory (reuses the K/V ring).
+  float* red = reinterpret_cast<float*>(smem);  // [4][16][D]
+  float* sm = red + kWarps * 16 * D;            // [4][16] m
+  float* sl = sm + kWarps * 16;                 // [4][16] l
+  const int r0 = lane >> 2, r1 = r0 + 8;
+  if ((lane & 3) == 0) {
+    sm[warp * 16 + r0] = m0; sm[warp * 16 + r1] = m1;
+    sl[warp * 16 + r0] = l0; sl[warp * 16 + r1] = l1;
+  }
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) {
+    const int c = i * 8 + (lane & 3) * 2;
+    red[(warp * 16 + r0) * D + c] = acc[i][0];
+    red[(warp * 16 + r0) * D + c + 1] = acc[i][1];
+    red[(warp * 16 + r1) * D + c] = acc[i][2];
+    red[(warp * 16 + r1) * D + c + 1] = acc[i][3];
+  }
+  __syncthreads();
+  for (int i = tid; i < G * D; i += kWarps * 32) {
+    const int r = i / D, c = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm[w * 16 + r]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = sm[w * 16 + r];
+      const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+      L += f * sl[w * 16 + r];
+      O += f * red[(w * 16 + r) * D + c];
+    }
+    const float out = L > 0.f ? O / L : 0.f;
+    if (p.n_splits == 1) {
+      T* o = static_cast<T*>(p.o);
+      o[seq * p.so_s + (kvh * G + r) * p.so_h + c] = from_f32<T>(out);
+    } else {
+      const int64_t pi = ((int64_t)seq * p.hkv + kvh) * p.n_splits + split;
+      p.part_o[(pi * 16 + r) * D + c] = out;
+      if (c == 0) p.part_lse[pi * 16 + r] = L > 0.f ? M + log2f(L) : -INFINITY;
+    }
+  }
+}
+
+// Merge split results: one CTA per (seq, q-head).
+template <typename T, int D>
+__global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeParams p) {
+  const int seq = blockIdx.y, hq = blockIdx.x;
+  const int kvh = hq / p.group, r = hq % p.group;
+  const int64_t base = ((int64_t)seq * p.hkv + kvh) * p.n_splits;
+  __shared__ float s_w[1024];
+  __shared__ float s_tot;
+  float M = -INFINITY;
+  for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, p.part_lse[(base + s) * 16 + r]);
+  float tot = 0.f;
+  for (int s = threadIdx.x; s < p.n_splits; s += blockDim.x) {
+    const float l = p.part_lse[(base + s) * 16 + r];
+    const float w = l == -INFINITY ? 0.f : exp2f(l - M);
+    s_w[s] = w;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.n_splits; ++s) tot += s_w[s];
+    s_tot = tot;
+  }
+  __syncthreads();
+  tot = s_tot;
+  T* o = static_cast<T*>(p.o);
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < p.n_splits; ++s)
+      if (s_w[s] != 0.f) acc += s_w[s] * p.part_o[((base + s) * 16 + r) * D + c];
+    o[seq * p.so_s + hq * p.so_h + c] = from_f32<T>(tot > 0.f ? acc / tot : 0.f);
+  }
+}
+
+}  // namespace
+
+constexpr int kMaxSplits = 1024;
+
+// Chooses the split length (a multiple of the tile) for a context bound and batch.
+inline int decode_split_len(int64_t n_seqs, int64_t hkv, int64_t max_ctx, int64_t max_splits) {
+  const int64_t per = n_seqs * hkv;
+  int64_t target = (8LL * 148 + per - 1) / (per > 0 ? per : 1);  // aim for >= 8 CTAs per SM of work
+  int64_t split = (max_ctx + target - 1) / (target > 0 ? target : 1);
+  split = ((split + kTile - 1) / kTile) * kTile;
+  if (split < 512) split = 512;
+  while ((max_ctx + split - 1) / split > max_splits) split += kTile;
+  return (int)split;
+}
+
+size_t decode_workspace_bytes(int64_t n_seqs, int64_t hkv, int64_t dv, int n_splits) {
+  if (n_splits <= 1) return 0;
+  return (size_t)n_seqs * hkv * n_splits * 16 * (dv + 1) * sizeof(float);
+}
+
+template <typename T, int D>
+int launch_decode(DecodeParams& p, int64_t n_seqs, cudaStream_t st) {
+  const int smem = DecodeSmem<D>::kBytes;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(paged_decode_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr_set = true;
+  }
+  dim3 grid(p.n_splits, p.hkv, (unsigned)n_seqs);
+  paged_decode_kernel<T, D><<<grid, kWarps * 32, smem, st>>>(p);
+  if (p.n_splits > 1) {
+    dim3 g2(p.hq, (unsigned)n_seqs);
+    paged_decode_merge_kernel<T, D><<<g2, 128, 0, st>>>(p);
+  }
+  return MVB_OK;
+}
+
+// Shared by the workspace and the static-scratch entry points.
+int run_paged_decode(const char* op, const mvb_tensor* q, const mvb_tensor* kc, const mvb_tensor* vc,
+                     const mvb_tensor* bt, const mvb_tensor* ctx, float scale, int block_size, int64_t max_ctx,
+                     mvb_tensor* o, void* ws, size_t ws_bytes, int64_t max_splits, cudaStream_t st) {
+  int rc;
+  if ((rc = check_tensor(q, op, "q", 3)) || (rc = check_tensor(kc, op, "k_cache", 4)) ||
+      (rc = check_tensor(vc, op, "v_cache", 4)) || (rc = check_tensor(bt, op, "block_tables", 2)) ||
+      (rc = check_tensor(ctx, op, "context_lens", 1)) || (rc = check_tensor(o, op, "o", 3)))
+    return rc;
+  const int64_t S = q->shape[0], hq = q->shape[1], d = q->shape[2];
+  const int64_t hkv = kc->shape[2], dv = vc->shape[3];
+  MVB_CHECK_ARG(kc->shape[1] == block_size && vc->shape[1] == block_size && block_size > 0,
+                "%s: caches must be [n_blocks, block_size=%d, Hkv, D]", op, block_size);
+  MVB_CHECK_ARG(kc->shape[3] == d && vc->shape[2] == hkv && vc->shape[0] == kc->shape[0],
+                "%s: k_cache/v_cache shapes disagree with q", op);
+  MVB_CHECK_ARG(hkv > 0 && hq % hkv == 0, "%s: Hq must be a multiple of Hkv", op);
+  MVB_CHECK_ARG(o->shape[0] == S && o->shape[1] == hq && o->shape[2] == dv, "%s: o must be [S, Hq, Dv]", op);
+  MVB_CHECK_ARG(bt->shape[0] >= S && ctx->shape[0] >= S && bt->dtype == MVB_I32 && ctx->dtype == MVB_I32,
+                "%s: block_tables [S, max_blocks] and context_lens [S] must be int32", op);
+  MVB_CHECK_ARG(q->dtype == kc->dtype && q->dtype == vc->dtype && q->dtype == o->dtype, "%s: dtype mismatch", op);
+  MVB_CHECK_SUPPORTED(q->dtype == MVB_BF16 || q->dtype == MVB_F16, "%s: q/k/v must be bf16 or fp16", op);
+  MVB_CHECK_SUPPORTED(d == dv && (d == 64 || d == 128 || d == 256), "%s: head dim must be 64, 128 or 256", op);
+  MVB_CHECK_SUPPORTED(hq / hkv <= 16, "%s: at most 16 query heads per kv head", op);
+  MVB_CHECK_SUPPORTED(q->stride[2] == 1 && o->stride[2] == 1 && kc->stride[3] == 1 && vc->stride[3] == 1 &&
+                          q->stride[1] % 8 == 0 && q->stride[0] % 8 == 0 && kc->stride[0] % 8 == 0 &&
+                          kc->stride[1] % 8 == 0 && kc->stride[2] % 8 == 0 && vc->stride[0] % 8 == 0 &&
+                          vc->stride[1] % 8 == 0 && vc->stride[2] % 8 == 0 && aligned16(q->data) &&
+                          aligned16(kc->data) && aligned16(vc->data),
+                      "%s: rows must be contiguous and 16-byte aligned", op);
+  MVB_CHECK_SUPPORTED(S <= 65535 && hkv <= 65535, "%s: too many sequences", op);
+  if (S == 0 || hq == 0) return MVB_OK;
+  if (max_ctx <= 0) max_ctx = bt->shape[1] * (int64_t)block_size;
+  if (max_ctx <= 0) max_ctx = 1;
+
+  DecodeParams p;
+  p.q = q->data; p.kc = kc->data; p.vc = vc->data;
+  p.bt = static_cast<const int32_t*>(bt->data); p.ctx = static_cast<const int32_t*>(ctx->data); p.o = o->data;
+  p.sq_s = q->stride[0]; p.sq_h = q->stride[1]; p.so_s = o->stride[0]; p.so_h = o->stride[1];
+  p.skc_b = kc->stride[0]; p.skc_t = kc->stride[1]; p.skc_h = kc->stride[2];
+  p.svc_b = vc->stride[0]; p.svc_t = vc->stride[1]; p.svc_h = vc->stride[2];
+  p.sbt_s = bt->stride[0]; p.sbt_b = bt->stride[1];
+  p.hq = (int)hq; p.hkv = (int)hkv; p.group = (int)(hq / hkv); p.block_size = block_size;
+  p.max_blocks = (int)bt->shape[1];
+  p.scale_log2 = scale * 1.4426950408889634f;
+
+  int split = decode_split_len(S, hkv, max_ctx, max_splits);
+  int n_splits = (int)((max_ctx + split - 1) / split);
+  if (ws == nullptr || ws_bytes < decode_workspace_bytes(S, hkv, dv, n_splits)) {
+    n_splits = 1;
+    split = (int)max_ctx;
+  }
+  p.n_splits = n_splits;
+  p.split_len = split;
+  p.part_o = n_splits > 1 ? static_cast<float*>(ws) : nullptr;
+  p.part_lse = n_splits > 1 ? p.part_o + (size_t)S * hkv * n_splits * 16 * dv : nullptr;
+
+  if (q->dtype == MVB_BF16) {
+    switch (d) {
+      case 64: launch_decode<__nv_bfloat16, 64>(p, S, st); break;
+      case 128: launch_decode<__nv_bfloat16, 128>(p, S, st); break;
+      case 256: launch_decode<__nv_bfloat16, 256>(p, S, st); break;
+    }
+  } else {
+    switch (d) {
+      case 64: launch_decode<__half, 64>(p, S, st); break;
+      case 128: launch_decode<__half, 128>(p, S, st); break;
+      case 256: launch_decode<__half, 256>(p, S, st); break;
+    }
+  }
+  MVB_CHECK_LAUNCH(op);
+  return MVB_OK;
+}
+
+}  // namespace mvb
+
+extern "C" size_t mvb_paged_attention_decode_workspace_size(int64_t n_seqs, int64_t num_kv_heads, int64_t head_v_dim,
+                                                            int64_t max_context_len) {
+  // Sized for the split policy run_paged_decode uses.
+  const int64_t hkv = num_kv_heads;
+  if (n_seqs <= 0 || hkv <= 0 || max_context_len <= 0) return 0;
+  const int split = mvb::decode_split_len(n_seqs, hkv, max_context_len, mvb::kMaxSplits);
+  const int n_splits = (int)((max_context_len + split - 1) / split);
+  return mvb::decode_workspace_bytes(n_seqs, hkv, head_v_dim, n_splits);
+}
+
+extern "C" int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor* k_cache, const mvb_tensor* v_cache,
+                                          const mvb_tensor* block_tables, const mvb_tensor* context_lens, float scale,
+                                          int block_size, int64_t max_context_len, mvb_tensor* o, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  return mvb::run_paged_decode("paged_attention_decode", q, k_cache, v_cache, block_tables, context_lens, scale,
+                               block_size, max_context_len, o, workspace, workspace_bytes, mvb::kMaxSplits,
+                               static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,26 @@
+"""Recurrent gated delta rule, one token per sequence (drop-in for
+``myvllm.ops.gated_delta_rule.fused_recurrent_gdn``, reference ``:105-166``)."""
+
+from __future__ import annotations
+
+import torch
+
+from ... import _lib
+
+
+def fused_recurrent_gdn(
+    q: torch.Tensor,  # (seq_cnt, num_k_heads, k_head_dim)
+    k: torch.Tensor,  # (seq_cnt, num_k_heads, k_head_dim)
+    v: torch.Tensor,  # (seq_cnt, num_v_heads, v_head_dim)
+    g: torch.Tensor,  # (seq_cnt, num_v_heads)   natural-log decay
+    beta: torch.Tensor,  # (seq_cnt, num_v_heads)
+    recurrent_state: torch.Tensor,  # (max_seq_cnt, num_v_heads, k_head_dim, v_head_dim) fp32, in place
+    recurrent_state_indices: torch.Tensor,  # (seq_cnt,)
+) -> torch.Tensor:
+    _lib.require_cuda("fused_recurrent_gdn", q, k, v, g, beta, recurrent_state, recurrent_state_indices)
+    idx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
+    o = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    _lib.call("fused_recurrent_gdn", "mvb_fused_recurrent_gdn", _lib.desc(q), _lib.desc(k), _lib.desc(v),
+              _lib.desc(g), _lib.desc(beta), _lib.desc(recurrent_state), _lib.desc(idx), _lib.desc(o),
+              float(k.shape[-1] ** -0.5), _lib.stream_of(q))
+    return o

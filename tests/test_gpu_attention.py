@@ -1,0 +1,169 @@
+"""GPU parity: varlen flash-attention prefill, paged decode, paged prefill and the
+paged KV write vs the oracle (and torch fp32 attention at full sizes)."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from myvllm_b200 import workloads as W
+from myvllm_b200.ops.full_attention import (flash_attention_prefill, paged_flash_attention_decode,
+                                            paged_flash_attention_prefill)
+from myvllm_b200.ops.kv_cache import store_kvcache
+from tests.util import assert_close, to_np
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+dev = "cuda"
+
+
+def _qkv(lens, hq, hkv, d, seed, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    T = sum(lens)
+    return (torch.randn(T, hq, d, generator=g).to(dtype), torch.randn(T, hkv, d, generator=g).to(dtype),
+            torch.randn(T, hkv, d, generator=g).to(dtype))
+
+
+@pytest.mark.parametrize("d", [64, 128, 256])
+@pytest.mark.parametrize("causal", [True, False])
+def test_varlen_prefill_vs_oracle(d, causal):
+    lens = [1, 17, 128, 129, 300, 0, 64]
+    q, k, v = _qkv(lens, 16, 2, d, seed=d)
+    cu = W.cu_from_lengths(lens, "cpu")
+    scale = d ** -0.5
+    o = flash_attention_prefill(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), scale, 16, 2, d, d, causal)
+    ref = oracle.attention.varlen(to_np(q), to_np(k), to_np(v), cu.numpy(), scale, causal)
+    assert_close(o, ref)
+
+
+def test_varlen_prefill_c3_full_size_vs_torch_fp32():
+    inp = W.c3_inputs(dev)
+    o = flash_attention_prefill(inp["q"], inp["k"], inp["v"], inp["cu"], inp["scale"], 16, 2, 256, 256, True)
+    cu = inp["cu"].tolist()
+    for s in (0, len(cu) - 2):
+        a, b = cu[s], cu[s + 1]
+        for h in (0, 9):
+            qf = inp["q"][a:b, h].float()[None]
+            kf = inp["k"][a:b, h // 8].float()[None]
+            vf = inp["v"][a:b, h // 8].float()[None]
+            ref = F.scaled_dot_product_attention(qf, kf, vf, is_causal=True, scale=inp["scale"])[0]
+            assert_close(o[a:b, h], ref, what=f"seq {s} head {h}")
+
+
+def _paged(lens_ctx, hkv, d, bs, seed, dtype=torch.bfloat16, extra_blocks=3):
+    g = torch.Generator().manual_seed(seed)
+    nb_per = [max(1, (n + bs - 1) // bs) for n in lens_ctx]
+    n_blocks = sum(nb_per) + extra_blocks
+    perm = torch.randperm(n_blocks, generator=g)
+    mb = max(nb_per)
+    bt = torch.full((len(lens_ctx), mb), -1, dtype=torch.int32)  # unused entries are garbage (-1)
+    o = 0
+    for s, nb in enumerate(nb_per):
+        bt[s, :nb] = perm[o:o + nb].to(torch.int32)
+        o += nb
+    kc = torch.randn(n_blocks, bs, hkv, d, generator=g).to(dtype)
+    vc = torch.randn(n_blocks, bs, hkv, d, generator=g).to(dtype)
+    return kc, vc, bt
+
+
+def test_paged_decode_golden():
+    z = np.load(os.path.join(GOLDEN, "paged_decode.npz"))
+    q, kc, vc = (torch.tensor(z[n]).to(torch.bfloat16) for n in ("q", "k_cache", "v_cache"))
+    bt, ctx = torch.tensor(z["block_tables"]), torch.tensor(z["context_lens"])
+    scale, bs = float(z["scale"]), int(z["block_size"])
+    o = paged_flash_attention_decode(q.to(dev), kc.to(dev), vc.to(dev), bt.to(dev), ctx.to(dev), scale, bs)
+    ref = oracle.attention.paged_decode(to_np(q), to_np(kc), to_np(vc), bt.numpy(), ctx.numpy(), scale)
+    assert_close(o, ref)
+    # and the reference kernel's own fp32 output, within bf16 input-rounding tolerance
+    assert np.abs(to_np(o) - z["ref_o"]).max() < 5e-2
+
+
+@pytest.mark.parametrize("hq,hkv", [(16, 2), (4, 1), (2, 1), (8, 8), (16, 1)])
+@pytest.mark.parametrize("d", [128, 256])
+def test_paged_decode_vs_oracle(hq, hkv, d):
+    ctx = [1, 255, 256, 257, 1000, 5000, 0, 63]
+    bs = 256
+    kc, vc, bt = _paged(ctx, hkv, d, bs, seed=hq + d)
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(len(ctx), hq, d, generator=g).to(torch.bfloat16)
+    ctx_t = torch.tensor(ctx, dtype=torch.int32)
+    o = paged_flash_attention_decode(q.to(dev), kc.to(dev), vc.to(dev), bt.to(dev), ctx_t.to(dev), d ** -0.5, bs)
+    ref = oracle.attention.paged_decode(to_np(q), to_np(kc), to_np(vc), bt.clamp_min(0).numpy(), ctx, d ** -0.5)
+    assert_close(o, ref)
+
+
+def test_paged_decode_small_block_and_unsplit():
+    ctx = [3, 40, 17]
+    kc, vc, bt = _paged(ctx, 2, 64, 16, seed=7)
+    q = torch.randn(3, 8, 64).to(torch.bfloat16)
+    o = paged_flash_attention_decode(q.to(dev), kc.to(dev), vc.to(dev), bt.to(dev),
+                                     torch.tensor(ctx, dtype=torch.int32, device=dev), 0.125, 16)
+    ref = oracle.attention.paged_decode(to_np(q), to_np(kc), to_np(vc), bt.clamp_min(0).numpy(), ctx, 0.125)
+    assert_close(o, ref)
+
+
+def test_paged_decode_c4_shapes_vs_torch_fp32():
+    """Config-4 attention shapes: 128 seqs, ctx ~U[1024, 32768], Hq=16, Hkv=2, D=256, block 256."""
+    ctx = W.seq_lengths(128, 1024, 32768, 4)
+    kc, vc, bt = _paged(ctx, 2, 256, 256, seed=4, extra_blocks=0)
+    q = torch.randn(128, 16, 256).to(torch.bfloat16).to(dev)
+    kc, vc, bt = kc.to(dev), vc.to(dev), bt.to(dev)
+    o = paged_flash_attention_decode(q, kc, vc, bt, torch.tensor(ctx, dtype=torch.int32, device=dev), 1 / 16, 256)
+    for s in (0, 77, 127):
+        n = ctx[s]
+        blocks = bt[s, torch.arange(n, device=dev) // 256].long()
+        kk = kc[blocks, torch.arange(n, device=dev) % 256].float()  # [n, 2, 256]
+        vv = vc[blocks, torch.arange(n, device=dev) % 256].float()
+        qq = q[s].float().view(2, 8, 256)
+        p = torch.softmax(torch.einsum("hgd,nhd->hgn", qq, kk) / 16, -1)
+        ref = torch.einsum("hgn,nhd->hgd", p, vv).reshape(16, 256)
+        assert_close(o[s], ref, what=f"seq {s}")
+
+
+def test_store_kvcache_exact():
+    T, hkv, d, bs, nb = 50, 2, 256, 16, 8
+    g = torch.Generator().manual_seed(0)
+    k = torch.randn(T, hkv, d, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, hkv, d, generator=g).to(torch.bfloat16)
+    slots = torch.randperm(nb * bs, generator=g)[:T].to(torch.int32)
+    slots[::7] = -1
+    kc = torch.zeros(nb, bs, hkv, d, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    kc_g, vc_g = kc.to(dev), vc.to(dev)
+    store_kvcache(k.to(dev), v.to(dev), kc_g, vc_g, slots.to(dev))
+    kr, vr = kc.float().numpy(), vc.float().numpy()
+    oracle.kv.store(k.float().numpy(), v.float().numpy(), kr, vr, slots.numpy())
+    assert np.array_equal(kc_g.float().cpu().numpy(), kr)
+    assert np.array_equal(vc_g.float().cpu().numpy(), vr)
+
+
+def test_c3_kv_write_then_paged_prefill_equals_varlen():
+    """Config-3 style: write K/V through slot_mapping into a permuted paged cache, then the
+    paged prefill over that cache must equal the varlen prefill (same causal math)."""
+    inp = W.c3_inputs(dev, lengths=[1000, 257, 2048, 5])
+    bs = inp["block_size"]
+    kc = torch.zeros(inp["n_blocks"], bs, 2, 256, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    store_kvcache(inp["k"], inp["v"], kc, vc, inp["slot_mapping"])
+    ctx = torch.tensor(inp["lengths"], dtype=torch.int32, device=dev)
+    o1 = paged_flash_attention_prefill(inp["q"], kc, vc, inp["block_tables"], ctx, inp["cu"], None, inp["scale"], bs)
+    o2 = flash_attention_prefill(inp["q"], inp["k"], inp["v"], inp["cu"], inp["scale"], 16, 2, 256, 256, True)
+    assert_close(o1, o2)
+
+
+def test_paged_prefill_with_prior_context_vs_oracle():
+    ctx = [300, 40, 513]
+    new = [20, 40, 1]
+    kc, vc, bt = _paged(ctx, 2, 128, 64, seed=13)
+    g = torch.Generator().manual_seed(2)
+    q = torch.randn(sum(new), 16, 128, generator=g).to(torch.bfloat16)
+    cu = W.cu_from_lengths(new, "cpu")
+    o = paged_flash_attention_prefill(q.to(dev), kc.to(dev), vc.to(dev), bt.to(dev),
+                                      torch.tensor(ctx, dtype=torch.int32, device=dev), cu.to(dev), None,
+                                      128 ** -0.5, 64)
+    ref = oracle.attention.paged_prefill(to_np(q), to_np(kc), to_np(vc), bt.clamp_min(0).numpy(), ctx, cu.numpy(),
+                                         128 ** -0.5)
+    assert_close(o, ref)

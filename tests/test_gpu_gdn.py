@@ -1,0 +1,152 @@
+"""GPU parity: gated delta rule (chunked prefill and recurrent decode) vs the oracle."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from myvllm_b200 import workloads as W
+from myvllm_b200.ops.gated_delta_rule.fused_recurrent_gdn import fused_recurrent_gdn
+from myvllm_b200.ops.gated_delta_rule.gated_delta_rule import chunk_gated_delta_rule, recurrent_gated_delta_rule
+from tests.util import assert_close, assert_state_close, state_rel_err, to_np
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+dev = "cuda"
+
+
+def _golden_c0():
+    d = np.load(os.path.join(GOLDEN, "c0_gdn.npz"))
+    t = {k: torch.tensor(d[k]).to(dev) for k in ["q", "k", "v", "g", "beta"]}
+    return d, t
+
+
+def test_c0_golden_prefill_entry_fp32():
+    """Config 0 through chunk_gated_delta_rule (fp32 inputs run the exact fp32 kernel)."""
+    d, t = _golden_c0()
+    state = torch.zeros(1, 4, 64, 64, device=dev)
+    o = chunk_gated_delta_rule(t["q"], t["k"], t["v"], t["g"], t["beta"], state,
+                               torch.zeros(1, dtype=torch.int32, device=dev),
+                               torch.tensor([0, 256], dtype=torch.int32, device=dev))
+    torch.cuda.synchronize()
+    assert np.abs(to_np(o) - d["ref_o"]).max() < 2e-5
+    assert np.abs(to_np(state[0]) - d["ref_state"]).max() < 2e-5
+
+
+def test_c0_golden_decode_stepwise():
+    """Config 0 as 256 decode steps of fused_recurrent_gdn (the reference's K12 op)."""
+    d, t = _golden_c0()
+    state = torch.zeros(1, 4, 64, 64, device=dev)
+    idx = torch.zeros(1, dtype=torch.int32, device=dev)
+    outs = []
+    for i in range(256):
+        outs.append(recurrent_gated_delta_rule(t["q"][i:i + 1], t["k"][i:i + 1], t["v"][i:i + 1], t["g"][i:i + 1],
+                                               t["beta"][i:i + 1], state, idx))
+    o = torch.cat(outs)
+    assert np.abs(to_np(o) - d["ref_o"]).max() < 2e-5
+    assert np.abs(to_np(state[0]) - d["ref_state"]).max() < 2e-5
+
+
+def _rand_gdn(lens, hk, hv, dk, dv, seed, dtype=torch.bfloat16, n_slots=None, state_scale=0.1):
+    g_ = torch.Generator().manual_seed(seed)
+    T = sum(lens)
+    q = torch.nn.functional.normalize(torch.randn(T, hk, dk, generator=g_), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(T, hk, dk, generator=g_), dim=-1)
+    v = torch.randn(T, hv, dv, generator=g_)
+    A_log = torch.empty(hv).uniform_(0, np.log(16), generator=g_)
+    dt = 0.1 * torch.randn(hv, generator=g_)
+    g, beta = W.gdn_gates(torch.randn(T, hv, generator=g_), torch.randn(T, hv, generator=g_), A_log, dt)
+    S = len(lens)
+    n_slots = n_slots or S + 3
+    state = state_scale * torch.randn(n_slots, hv, dk, dv, generator=g_)
+    idx = torch.randperm(n_slots, generator=g_)[:S].to(torch.int32)
+    cu = W.cu_from_lengths(lens, "cpu")
+    return dict(q=q.to(dtype), k=k.to(dtype), v=v.to(dtype), g=g, beta=beta, state=state, idx=idx, cu=cu)
+
+
+def _to(d, device):
+    return {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
+
+
+@pytest.mark.parametrize("lens", [[1, 63, 64, 65, 0, 200, 129], [64], [1], [513, 7]])
+def test_chunk_bf16_vs_oracle(lens):
+    cpu = _rand_gdn(lens, 2, 4, 128, 128, seed=len(lens))
+    gpu = _to(cpu, dev)
+    o = chunk_gated_delta_rule(gpu["q"], gpu["k"], gpu["v"], gpu["g"], gpu["beta"], gpu["state"], gpu["idx"],
+                               gpu["cu"])
+    st = cpu["state"].double().numpy()
+    ref = oracle.gdn.chunked(to_np(cpu["q"]), to_np(cpu["k"]), to_np(cpu["v"]), to_np(cpu["g"]), to_np(cpu["beta"]),
+                             st, cpu["idx"].numpy(), cpu["cu"].numpy(), 64)
+    assert_close(o, ref, what="o")
+    assert_state_close(gpu["state"], st)
+
+
+def test_chunk_continuation_equals_single_call():
+    """A prefill split in two calls (state carried through the cache slot) equals one call."""
+    lens = [300, 77]
+    cpu = _rand_gdn(lens, 2, 4, 128, 128, seed=11)
+    a, b = _to(cpu, dev), _to(cpu, dev)
+    o1 = chunk_gated_delta_rule(a["q"], a["k"], a["v"], a["g"], a["beta"], a["state"], a["idx"], a["cu"])
+    # second run: first 100 tokens of every sequence, then the rest
+    cu = cpu["cu"].tolist()
+    first = [list(range(cu[s], cu[s] + 100)) for s in range(2)]
+    rest = [list(range(cu[s] + 100, cu[s + 1])) for s in range(2)]
+    outs = torch.empty_like(o1)
+    for part in (first, rest):
+        ids = torch.tensor(sum(part, []), device=dev)
+        cu_p = W.cu_from_lengths([len(p) for p in part], dev)
+        op = chunk_gated_delta_rule(b["q"][ids], b["k"][ids], b["v"][ids], b["g"][ids], b["beta"][ids], b["state"],
+                                    b["idx"], cu_p)
+        outs[ids] = op
+    assert_close(outs, o1, what="o (split vs single)")
+    assert_state_close(b["state"], a["state"], what="state (split vs single)")
+
+
+def test_chunk_c1_shapes_vs_fp32_recurrent_kernel():
+    """Config-1 head layout (16 k-heads / 32 v-heads x 128) at full config-1 lengths: the
+    bf16 tensor-core chunk kernel against the exact fp32 token-serial kernel on the same
+    inputs (a size-independent check: both compute the same recurrence)."""
+    lens = W.seq_lengths(8, 512, 8192, 0)
+    cpu = _rand_gdn(lens, 16, 32, 128, 128, seed=5, n_slots=8, state_scale=0.0)
+    a = _to(cpu, dev)
+    b = {k: (v.float() if isinstance(v, torch.Tensor) and v.dtype == torch.bfloat16 else v) for k, v in a.items()}
+    b["state"] = a["state"].clone()
+    o_fast = chunk_gated_delta_rule(a["q"], a["k"], a["v"], a["g"], a["beta"], a["state"], a["idx"], a["cu"])
+    o_ref = chunk_gated_delta_rule(b["q"], b["k"], b["v"], b["g"], b["beta"], b["state"], b["idx"], b["cu"])
+    assert_close(o_fast, o_ref, what="o (chunk bf16 vs recurrent fp32)")
+    assert_state_close(a["state"], b["state"])
+
+
+def test_decode_bf16_vs_oracle():
+    S, hk, hv = 24, 16, 32
+    cpu = _rand_gdn([1] * S, hk, hv, 128, 128, seed=3, n_slots=40)
+    gpu = _to(cpu, dev)
+    o = fused_recurrent_gdn(gpu["q"], gpu["k"], gpu["v"], gpu["g"], gpu["beta"], gpu["state"], gpu["idx"])
+    st = cpu["state"].double().numpy()
+    ref = oracle.gdn.recurrent_step(to_np(cpu["q"]), to_np(cpu["k"]), to_np(cpu["v"]), to_np(cpu["g"]),
+                                    to_np(cpu["beta"]), st, cpu["idx"].numpy())
+    assert_close(o, ref, what="o")
+    assert state_rel_err(gpu["state"], st) < 1e-5  # fp32 math throughout
+
+
+def test_decode_c2_full_size_sampled():
+    """Config 2 at full size (256 seqs, state [256,32,128,128]); 12 sequences are checked
+    against the oracle, and untouched slots must stay bit-identical."""
+    inp = W.c2_inputs(dev)
+    q, k, v = W.split_qkv(inp["x"])
+    q, k = W.l2norm(q), W.l2norm(k)
+    extra = torch.randn(4, 32, 128, 128, device=dev)  # slots not addressed by idx
+    state = torch.cat([inp["state"], extra])
+    before = state.clone()
+    o = fused_recurrent_gdn(q, k, v, inp["g"], inp["beta"], state, inp["idx"])
+    torch.cuda.synchronize()
+    assert torch.equal(state[256:], before[256:])
+    pick = torch.arange(0, 256, 23)
+    idx = inp["idx"][pick].cpu().numpy()
+    st = before.cpu().double().numpy()
+    ref = oracle.gdn.recurrent_step(to_np(q[pick]), to_np(k[pick]), to_np(v[pick]), to_np(inp["g"][pick]),
+                                    to_np(inp["beta"][pick]), st, idx)
+    assert_close(o[pick], ref, what="o")
+    assert state_rel_err(state[idx], st[idx]) < 1e-5
