@@ -83,19 +83,21 @@ int mvb_causal_conv1d_update(const mvb_tensor* x, const mvb_tensor* weight, mvb_
 /* Chunked gated delta rule (prefill).  q,k [T, Hk, K]; v [T, Hv, V]; g, beta [T, Hv]
  * (g = natural-log decay); recurrent_state [S_max, Hv, K, V] fp32 -- the rows
  * recurrent_state_indices[s] are read as the initial state and overwritten with the
- * final state; cu_seqlens [S+1]; o [T, Hv, V] (dtype of v).  scale <= 0 means K^-0.5. */
+ * final state; cu_seqlens [S+1]; o [T, Hv, V] (dtype of v).  scale <= 0 means K^-0.5.
+ * use_qk_l2norm != 0 applies the layer's q/k L2 normalisation (x * rsqrt(sum x^2 + 1e-6),
+ * m/layers/linear_attention.py:113-114) inside the kernel. */
 int mvb_chunk_gated_delta_rule(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                                const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,
                                const mvb_tensor* recurrent_state_indices, const mvb_tensor* cu_seqlens,
-                               mvb_tensor* o, float scale, void* stream);
+                               mvb_tensor* o, float scale, int use_qk_l2norm, void* stream);
 
 /* Recurrent gated delta rule, one token per sequence (decode).  q,k [S, Hk, K];
  * v [S, Hv, V]; g, beta [S, Hv]; state [S_max, Hv, K, V] fp32 updated in place;
- * o [S, Hv, V].  scale <= 0 means K^-0.5. */
+ * o [S, Hv, V].  scale <= 0 means K^-0.5; use_qk_l2norm as above. */
 int mvb_fused_recurrent_gdn(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                             const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,
                             const mvb_tensor* recurrent_state_indices, mvb_tensor* o, float scale,
-                            void* stream);
+                            int use_qk_l2norm, void* stream);
 
 /* Varlen (optionally causal) attention.  q [T, Hq, D]; k [T, Hkv, D]; v [T, Hkv, Dv];
  * cu_seqlens [S+1]; o [T, Hq, Dv] (dtype of q).  bf16/f16 only. */

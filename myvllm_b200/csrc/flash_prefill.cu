@@ -320,8 +320,8 @@ extern "C" int mvb_flash_attention_prefill(const mvb_tensor* q, const mvb_tensor
                           aligned16(k->data) && aligned16(v->data) &&
                           (reinterpret_cast<uintptr_t>(o->data) & 3) == 0,
                       "%s: rows must be contiguous and 16-byte aligned", op);
-  MVB_CHECK_SUPPORTED(num_heads <= 65535, "%s: too many heads", op);
   const int64_t n_seqs = cu_seqlens->shape[0] - 1;
+  MVB_CHECK_SUPPORTED(num_heads <= 65535 && (T + 127) / 128 + n_seqs <= 65535, "%s: too many heads or tokens", op);
   if (T == 0 || n_seqs == 0 || num_heads == 0) return MVB_OK;
   FaParams p;
   p.q = q->data; p.k = k->data; p.v = v->data; p.o = o->data;
@@ -372,6 +372,7 @@ extern "C" int mvb_paged_attention_prefill(const mvb_tensor* q, const mvb_tensor
                           aligned16(q->data) && aligned16(k_cache->data) && aligned16(v_cache->data) &&
                           (reinterpret_cast<uintptr_t>(o->data) & 3) == 0,
                       "%s: rows must be contiguous and 16-byte aligned", op);
+  MVB_CHECK_SUPPORTED(hq <= 65535 && (T + 127) / 128 + n_seqs <= 65535, "%s: too many heads or tokens", op);
   if (T == 0 || n_seqs == 0 || hq == 0) return MVB_OK;
   FaParams p;
   p.q = q->data; p.k = k_cache->data; p.v = v_cache->data; p.o = o->data;

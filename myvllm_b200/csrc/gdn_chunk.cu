@@ -13,11 +13,18 @@
 //   u      = (Ti diag(beta)) v,   w = (Ti diag(beta e^G)) k
 //   v_new  = u - w S;   o = scale (e^G (q S) + Aqk v_new)
 //   S     <- e^{G_last} S + k^T (e^{G_last - G} v_new)   (S: fp32 registers, bf16 copy in smem)
-// Contractions run on mma.sync m16n8k16 (bf16/f16 operands, fp32 accumulate); 8 warps,
-// each owning a 16-row x 64-column slab (or 16 state rows x 128 columns for the update).
+// Numerics: every contraction runs with fp16 operands and fp32 accumulation.  bf16 q/k/v
+// tiles are converted to fp16 in shared memory right after they land (exact for
+// 6e-5 < |x| < 65504), optionally L2-normalising q and k rows in the same pass; the
+// internal operands (Ti, w, the state copy, v_new) are then rounded to fp16 (2^-11)
+// instead of bf16 (2^-8), which keeps the final fp32 state within 1e-3 relative of the
+// exact recurrence.  Contractions run on mma.sync m16n8k16; 8 warps, each owning a
+// 16-row x 64-column slab (or 16 state rows x 128 columns for the update).
 //
 // Scheduling: a persistent grid; chains are handed out longest sequence first (the rank
 // of each sequence is computed on device) so the longest serial chain starts at once.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace mvb {
@@ -27,7 +34,7 @@ int check_gdn(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
               const mvb_tensor* o, int64_t* n_seqs_out);
 int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                   const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx,
-                  const mvb_tensor* cu, mvb_tensor* o, float scale, cudaStream_t st);
+                  const mvb_tensor* cu, mvb_tensor* o, float scale, int l2norm, cudaStream_t st);
 
 namespace {
 
@@ -59,7 +66,7 @@ struct ChunkParams {
   const int32_t* cu;
   int64_t sq_t, sq_h, sk_t, sk_h, sv_t, sv_h, so_t, so_h, sg_t, sg_h, sb_t, sb_h;
   int64_t ss_n, ss_h, ss_k;
-  int n_seqs, hk, hv;
+  int n_seqs, hk, hv, l2norm;
   float scale;
 };
 
@@ -114,8 +121,48 @@ __device__ __forceinline__ void st2(char* base, int off, float a, float b) {
   *reinterpret_cast<uint32_t*>(base + off) = pack2<T>(a, b);
 }
 
+// In place: 16-bit input tile rows -> fp16, q/k rows optionally scaled by
+// rsqrt(sum x^2 + 1e-6) (m/layers/linear_attention.py:113-114).  4 threads per row.
+template <typename T>
+__device__ __forceinline__ void convert_tiles(char* sQ, char* sK, char* sV, bool l2norm, int tid) {
+  const int r = tid >> 2, qq = tid & 3;  // row, quarter (4 chunks of 8)
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    char* base = m == 0 ? sQ : sK;
+    float f[4][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      unpack8<T>(*reinterpret_cast<const uint4*>(base + sw256(r, qq * 4 + i)), f[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[i][j] * f[i][j];
+    }
+    float sc = 1.f;
+    if (l2norm) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      sc = rsqrtf(ss + 1e-6f);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[i][j] *= sc;
+      *reinterpret_cast<uint4*>(base + sw256(r, qq * 4 + i)) = pack8<__half>(f[i]);
+    }
+  }
+  if constexpr (!std::is_same<T, __half>::value) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float f[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(sV + sw256(r, qq * 4 + i)), f);
+      *reinterpret_cast<uint4*>(sV + sw256(r, qq * 4 + i)) = pack8<__half>(f);
+    }
+  }
+}
+
 template <typename T, typename TG>
 __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
+  using CT = __half;  // compute (MMA operand) type
   extern __shared__ __align__(128) char smem[];
   char* sQ = smem + OFF_Q;
   char* sK = smem + OFF_K;
@@ -178,8 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
       const float2 lo = *reinterpret_cast<const float2*>(gstate + (warp * 16 + qr) * p.ss_k + col);
       const float2 hi = *reinterpret_cast<const float2*>(gstate + (warp * 16 + qr + 8) * p.ss_k + col);
       Sr[nf][0] = lo.x; Sr[nf][1] = lo.y; Sr[nf][2] = hi.x; Sr[nf][3] = hi.y;
-      st2<T>(sS, elem<256>(warp * 16 + qr, col), lo.x, lo.y);
-      st2<T>(sS, elem<256>(warp * 16 + qr + 8, col), hi.x, hi.y);
+      st2<CT>(sS, elem<256>(warp * 16 + qr, col), lo.x, lo.y);
+      st2<CT>(sS, elem<256>(warp * 16 + qr + 8, col), hi.x, hi.y);
     }
 
     for (int c0 = t_begin; c0 < t_end; c0 += C) {
@@ -213,6 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
       }
       cp_async_wait<0>();
       __syncthreads();
+      convert_tiles<T>(sQ, sK, sV, p.l2norm != 0, tid);
+      __syncthreads();
 
       // ---- step 1: A = k k^T, Aqk = q k^T  (warp: rows 16 mt, cols 32 nh) ----
       {
@@ -230,10 +279,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
           for (int np = 0; np < 2; ++np) {
             uint32_t b[4];
             ldb_nk<256>(b, sK, nh * 32 + np * 16, kc * 16, lane);
-            mma16816<T>(akk[np * 2], ak, b);
-            mma16816<T>(akk[np * 2 + 1], ak, b + 2);
-            mma16816<T>(aqk[np * 2], aq, b);
-            mma16816<T>(aqk[np * 2 + 1], aq, b + 2);
+            mma16816<CT>(akk[np * 2], ak, b);
+            mma16816<CT>(akk[np * 2 + 1], ak, b + 2);
+            mma16816<CT>(aqk[np * 2], aq, b);
+            mma16816<CT>(aqk[np * 2 + 1], aq, b + 2);
           }
         }
 #pragma unroll
@@ -250,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
             *reinterpret_cast<float2*>(sA + i * C + j) = make_float2(a0, a1);
             const float q0 = i >= j ? aqk[nf][hf * 2] * d0 : 0.f;
             const float q1 = i >= j + 1 ? aqk[nf][hf * 2 + 1] * d1 : 0.f;
-            st2<T>(sAqk, elem<128>(i, j), q0, q1);
+            st2<CT>(sAqk, elem<128>(i, j), q0, q1);
           }
         }
       }
@@ -268,13 +317,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
           t[i] = acc;
         }
         const float bu = sB[c], bw = sB[c] * exp2f(sG[c]);
-        T* tu = reinterpret_cast<T*>(sTu);
-        T* tw = reinterpret_cast<T*>(sTw);
+        CT* tu = reinterpret_cast<CT*>(sTu);
+        CT* tw = reinterpret_cast<CT*>(sTw);
 #pragma unroll
         for (int i = 0; i < C; ++i) {
           const int off = elem<128>(i, c) >> 1;
-          tu[off] = from_f32<T>(t[i] * bu);
-          tw[off] = from_f32<T>(t[i] * bw);
+          tu[off] = from_f32<CT>(t[i] * bu);
+          tw[off] = from_f32<CT>(t[i] * bw);
         }
       }
       __syncthreads();
@@ -297,18 +346,18 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
             uint32_t bv[4], bk[4];
             ldb_kn<256>(bv, sV, kc * 16, nh * 64 + np * 16, lane);
             ldb_kn<256>(bk, sK, kc * 16, nh * 64 + np * 16, lane);
-            mma16816<T>(u[np * 2], au, bv);
-            mma16816<T>(u[np * 2 + 1], au, bv + 2);
-            mma16816<T>(w[np * 2], aw, bk);
-            mma16816<T>(w[np * 2 + 1], aw, bk + 2);
+            mma16816<CT>(u[np * 2], au, bv);
+            mma16816<CT>(u[np * 2 + 1], au, bv + 2);
+            mma16816<CT>(w[np * 2], aw, bk);
+            mma16816<CT>(w[np * 2 + 1], aw, bk + 2);
           }
         }
         __syncthreads();  // sA is dead: w may overwrite it
 #pragma unroll
         for (int nf = 0; nf < 8; ++nf) {
           const int col = nh * 64 + nf * 8 + qc;
-          st2<T>(sW, elem<256>(mt * 16 + qr, col), w[nf][0], w[nf][1]);
-          st2<T>(sW, elem<256>(mt * 16 + qr + 8, col), w[nf][2], w[nf][3]);
+          st2<CT>(sW, elem<256>(mt * 16 + qr, col), w[nf][0], w[nf][1]);
+          st2<CT>(sW, elem<256>(mt * 16 + qr + 8, col), w[nf][2], w[nf][3]);
         }
       }
       __syncthreads();
@@ -330,10 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
           for (int np = 0; np < 4; ++np) {
             uint32_t b[4];
             ldb_kn<256>(b, sS, kc * 16, nh * 64 + np * 16, lane);
-            mma16816<T>(ws[np * 2], aw, b);
-            mma16816<T>(ws[np * 2 + 1], aw, b + 2);
-            mma16816<T>(o[np * 2], aq, b);
-            mma16816<T>(o[np * 2 + 1], aq, b + 2);
+            mma16816<CT>(ws[np * 2], aw, b);
+            mma16816<CT>(ws[np * 2 + 1], aw, b + 2);
+            mma16816<CT>(o[np * 2], aq, b);
+            mma16816<CT>(o[np * 2 + 1], aq, b + 2);
           }
         }
         const int i0 = mt * 16 + qr, i1 = i0 + 8;
@@ -345,10 +394,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
           const int col = nh * 64 + nf * 8 + qc;
           const float v00 = u[nf][0] - ws[nf][0], v01 = u[nf][1] - ws[nf][1];
           const float v10 = u[nf][2] - ws[nf][2], v11 = u[nf][3] - ws[nf][3];
-          st2<T>(sVn, elem<256>(i0, col), v00, v01);
-          st2<T>(sVn, elem<256>(i1, col), v10, v11);
-          st2<T>(sVp, elem<256>(i0, col), v00 * el0, v01 * el0);
-          st2<T>(sVp, elem<256>(i1, col), v10 * el1, v11 * el1);
+          st2<CT>(sVn, elem<256>(i0, col), v00, v01);
+          st2<CT>(sVn, elem<256>(i1, col), v10, v11);
+          st2<CT>(sVp, elem<256>(i0, col), v00 * el0, v01 * el0);
+          st2<CT>(sVp, elem<256>(i1, col), v10 * el1, v11 * el1);
           o[nf][0] *= eg0; o[nf][1] *= eg0; o[nf][2] *= eg1; o[nf][3] *= eg1;
         }
       }
@@ -364,8 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
           for (int np = 0; np < 4; ++np) {
             uint32_t b[4];
             ldb_kn<256>(b, sVn, kc * 16, nh * 64 + np * 16, lane);
-            mma16816<T>(o[np * 2], a, b);
-            mma16816<T>(o[np * 2 + 1], a, b + 2);
+            mma16816<CT>(o[np * 2], a, b);
+            mma16816<CT>(o[np * 2 + 1], a, b + 2);
           }
         }
         const int i0 = mt * 16 + qr, i1 = i0 + 8;
@@ -397,8 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
           for (int np = 0; np < 8; ++np) {
             uint32_t b[4];
             ldb_kn<256>(b, sVp, kc * 16, np * 16, lane);
-            mma16816<T>(Sr[np * 2], a, b);
-            mma16816<T>(Sr[np * 2 + 1], a, b + 2);
+            mma16816<CT>(Sr[np * 2], a, b);
+            mma16816<CT>(Sr[np * 2 + 1], a, b + 2);
           }
         }
       }
@@ -406,8 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_kernel(ChunkParams p) {
 #pragma unroll
       for (int nf = 0; nf < 16; ++nf) {
         const int col = nf * 8 + qc;
-        st2<T>(sS, elem<256>(warp * 16 + qr, col), Sr[nf][0], Sr[nf][1]);
-        st2<T>(sS, elem<256>(warp * 16 + qr + 8, col), Sr[nf][2], Sr[nf][3]);
+        st2<CT>(sS, elem<256>(warp * 16 + qr, col), Sr[nf][0], Sr[nf][1]);
+        st2<CT>(sS, elem<256>(warp * 16 + qr + 8, col), Sr[nf][2], Sr[nf][3]);
       }
       // the next chunk's loads are issued after this point; sS is read only after its
       // __syncthreads, so no extra barrier is needed here
@@ -440,7 +489,7 @@ void launch_chunk(const ChunkParams& p, cudaStream_t st) {
 
 int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
               const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
-              mvb_tensor* o, float scale, cudaStream_t st) {
+              mvb_tensor* o, float scale, int l2norm, cudaStream_t st) {
   if (cu == nullptr) MVB_FAIL(MVB_ERR_ARG, "%s: cu_seqlens is NULL", op);
   int64_t n_seqs = 0;
   int rc = check_gdn(op, q, k, v, g, beta, state, idx, cu, o, &n_seqs);
@@ -455,7 +504,7 @@ int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
                     (reinterpret_cast<uintptr_t>(state->data) & 7) == 0 && cu->dtype == MVB_I32 &&
                     cu->shape[0] >= 1 && (g->dtype == MVB_F32 || g->dtype == q->dtype);
   if (!fast)  // fp32 / other head sizes: token-serial recurrence (exact fp32 math)
-    return run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, st);
+    return run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, st);
   if (n_seqs == 0 || v->shape[1] == 0) return MVB_OK;
   ChunkParams p;
   p.q = q->data; p.k = k->data; p.v = v->data; p.g = g->data; p.beta = beta->data; p.o = o->data;
@@ -466,7 +515,7 @@ int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
   p.sv_t = v->stride[0]; p.sv_h = v->stride[1]; p.so_t = o->stride[0]; p.so_h = o->stride[1];
   p.sg_t = g->stride[0]; p.sg_h = g->stride[1]; p.sb_t = beta->stride[0]; p.sb_h = beta->stride[1];
   p.ss_n = state->stride[0]; p.ss_h = state->stride[1]; p.ss_k = state->stride[2];
-  p.n_seqs = (int)n_seqs; p.hk = (int)q->shape[1]; p.hv = (int)v->shape[1];
+  p.n_seqs = (int)n_seqs; p.hk = (int)q->shape[1]; p.hv = (int)v->shape[1]; p.l2norm = l2norm ? 1 : 0;
   p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)KD);
   const bool g32 = g->dtype == MVB_F32;
   if (q->dtype == MVB_BF16) {
@@ -485,7 +534,7 @@ int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
 extern "C" int mvb_chunk_gated_delta_rule(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                                           const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,
                                           const mvb_tensor* recurrent_state_indices, const mvb_tensor* cu_seqlens,
-                                          mvb_tensor* o, float scale, void* stream) {
+                                          mvb_tensor* o, float scale, int use_qk_l2norm, void* stream) {
   return mvb::run_chunk("chunk_gated_delta_rule", q, k, v, g, beta, recurrent_state, recurrent_state_indices,
-                        cu_seqlens, o, scale, static_cast<cudaStream_t>(stream));
+                        cu_seqlens, o, scale, use_qk_l2norm, static_cast<cudaStream_t>(stream));
 }

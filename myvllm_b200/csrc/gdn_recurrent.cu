@@ -13,9 +13,10 @@
 // Rows of one warp cover whole 256-byte (VS=64) row segments: coalesced 16-byte
 // streaming loads/stores (evict-first, the state is touched once per step).
 //
-// The same kernel with a token loop (tokens_from_cu = true) runs a whole packed
-// prefill sequence token by token with S in registers; the library uses it for fp32
-// inputs and head sizes the chunked tensor-core kernel does not cover.
+// The same kernel with a token loop (cu_seqlens given) runs a whole packed prefill
+// sequence token by token with S in registers; the library uses it for fp32 inputs and
+// head sizes the chunked tensor-core kernel does not cover.  With l2norm set, q and k
+// are scaled by rsqrt(sum x^2 + 1e-6) first (m/layers/linear_attention.py:113-114).
 #include "common.cuh"
 
 namespace mvb {
@@ -30,7 +31,7 @@ struct RecParams {
   int64_t sq_t, sq_h, sq_d, sk_t, sk_h, sk_d, sv_t, sv_h, sv_d, so_t, so_h, so_d;
   int64_t sg_t, sg_h, sb_t, sb_h;
   int64_t ss_n, ss_h, ss_k;  // state strides (V stride must be 1)
-  int hk, hv, vdim;
+  int hk, hv, vdim, l2norm;
   float scale;
 };
 
@@ -48,6 +49,7 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(RecParams p) {
   __shared__ float4 red_a[NW][32], red_b[NW][32];
   __shared__ float red_qk[NW][32];
   __shared__ float s_gb[2];
+  __shared__ float s_nrm[2];
 
   const int tid = threadIdx.x;
   const int cg = tid % CG;
@@ -95,6 +97,28 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(RecParams p) {
       s_gb[1] = to_f32<TG>(bp[t * p.sb_t + h * p.sb_h]);
     }
     __syncthreads();
+    if (p.l2norm) {
+      if (warp == 0) {
+        float a2 = 0.f, b2 = 0.f;
+        for (int i = lane; i < K; i += 32) {
+          a2 += sq[i] * sq[i];
+          b2 += sk[i] * sk[i];
+        }
+        a2 = warp_sum(a2);
+        b2 = warp_sum(b2);
+        if (lane == 0) {
+          s_nrm[0] = rsqrtf(a2 + 1e-6f);
+          s_nrm[1] = rsqrtf(b2 + 1e-6f);
+        }
+      }
+      __syncthreads();
+      const float nq = s_nrm[0], nk = s_nrm[1];
+      for (int i = tid; i < K; i += kThreads) {
+        sq[i] *= nq;
+        sk[i] *= nk;
+      }
+      __syncthreads();
+    }
 
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
     float qk = 0.f;
@@ -223,7 +247,7 @@ int check_gdn(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
 
 int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                   const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx,
-                  const mvb_tensor* cu, mvb_tensor* o, float scale, cudaStream_t st) {
+                  const mvb_tensor* cu, mvb_tensor* o, float scale, int l2norm, cudaStream_t st) {
   int64_t n_seqs = 0;
   int rc = check_gdn(op, q, k, v, g, beta, state, idx, cu, o, &n_seqs);
   if (rc) return rc;
@@ -245,7 +269,7 @@ int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, cons
   p.so_t = o->stride[0]; p.so_h = o->stride[1]; p.so_d = o->stride[2];
   p.sg_t = g->stride[0]; p.sg_h = g->stride[1]; p.sb_t = beta->stride[0]; p.sb_h = beta->stride[1];
   p.ss_n = state->stride[0]; p.ss_h = state->stride[1]; p.ss_k = state->stride[2];
-  p.hk = (int)hk; p.hv = (int)hv; p.vdim = (int)vd;
+  p.hk = (int)hk; p.hv = (int)hv; p.vdim = (int)vd; p.l2norm = l2norm ? 1 : 0;
   p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)kd);
 
   int r = MVB_OK;
@@ -265,7 +289,7 @@ int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, cons
 extern "C" int mvb_fused_recurrent_gdn(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                                        const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,
                                        const mvb_tensor* recurrent_state_indices, mvb_tensor* o, float scale,
-                                       void* stream) {
+                                       int use_qk_l2norm, void* stream) {
   return mvb::run_recurrent("fused_recurrent_gdn", q, k, v, g, beta, recurrent_state, recurrent_state_indices,
-                            nullptr, o, scale, static_cast<cudaStream_t>(stream));
+                            nullptr, o, scale, use_qk_l2norm, static_cast<cudaStream_t>(stream));
 }

@@ -16,11 +16,13 @@ def fused_recurrent_gdn(
     beta: torch.Tensor,  # (seq_cnt, num_v_heads)
     recurrent_state: torch.Tensor,  # (max_seq_cnt, num_v_heads, k_head_dim, v_head_dim) fp32, in place
     recurrent_state_indices: torch.Tensor,  # (seq_cnt,)
+    *,
+    use_qk_l2norm_in_kernel: bool = False,
 ) -> torch.Tensor:
     _lib.require_cuda("fused_recurrent_gdn", q, k, v, g, beta, recurrent_state, recurrent_state_indices)
     idx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
     o = torch.empty(v.shape, dtype=v.dtype, device=v.device)
     _lib.call("fused_recurrent_gdn", "mvb_fused_recurrent_gdn", _lib.desc(q), _lib.desc(k), _lib.desc(v),
               _lib.desc(g), _lib.desc(beta), _lib.desc(recurrent_state), _lib.desc(idx), _lib.desc(o),
-              float(k.shape[-1] ** -0.5), _lib.stream_of(q))
+              float(k.shape[-1] ** -0.5), int(use_qk_l2norm_in_kernel), _lib.stream_of(q))
     return o

@@ -40,7 +40,12 @@ def chunk_gated_delta_rule(
     recurrent_state: torch.Tensor,  # (max_seq_cnt, num_v_heads, k_head_dim, v_head_dim) fp32, in place
     recurrent_state_indices: torch.Tensor,  # (seq_cnt,)
     cu_seqlens: torch.Tensor,  # (seq_cnt + 1,)
+    *,
+    use_qk_l2norm_in_kernel: bool = False,
 ) -> torch.Tensor:
+    """``use_qk_l2norm_in_kernel`` folds the layer's q/k L2 norm (``linear_attention.py:113-114``)
+    into the kernel's tile load; the default keeps the reference contract (q, k normalised
+    by the caller)."""
     _lib.require_cuda("chunk_gated_delta_rule", q, k, v, g, beta, recurrent_state, recurrent_state_indices,
                       cu_seqlens)
     idx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
@@ -48,7 +53,7 @@ def chunk_gated_delta_rule(
     o = torch.empty(v.shape, dtype=v.dtype, device=v.device)
     _lib.call("chunk_gated_delta_rule", "mvb_chunk_gated_delta_rule", _lib.desc(q), _lib.desc(k), _lib.desc(v),
               _lib.desc(g), _lib.desc(beta), _lib.desc(recurrent_state), _lib.desc(idx), _lib.desc(cu),
-              _lib.desc(o), float(k.shape[-1] ** -0.5), _lib.stream_of(q))
+              _lib.desc(o), float(k.shape[-1] ** -0.5), int(use_qk_l2norm_in_kernel), _lib.stream_of(q))
     return o
 
 
@@ -60,6 +65,9 @@ def recurrent_gated_delta_rule(
     beta: torch.Tensor,
     recurrent_state: torch.Tensor,
     recurrent_state_indices: torch.Tensor,
+    *,
+    use_qk_l2norm_in_kernel: bool = False,
 ) -> torch.Tensor:
     """Decode: one token per sequence (reference ``gated_delta_rule.py:69-92``)."""
-    return fused_recurrent_gdn(q, k, v, g, beta, recurrent_state, recurrent_state_indices)
+    return fused_recurrent_gdn(q, k, v, g, beta, recurrent_state, recurrent_state_indices,
+                               use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)

@@ -67,7 +67,7 @@ def test_rejects_wrong_rank():
     bad = _fake([4, 2])
     rc, msg = _status("mvb_fused_recurrent_gdn", q, q, bad, _fake([4, 2], _lib.MVB_F32),
                       _fake([4, 2], _lib.MVB_F32), _fake([4, 2, 128, 128], _lib.MVB_F32),
-                      _fake([4], _lib.MVB_I32), _fake([4, 2, 128]), ctypes.c_float(0.0), None)
+                      _fake([4], _lib.MVB_I32), _fake([4, 2, 128]), ctypes.c_float(0.0), 0, None)
     assert rc == 1 and "v must have 3 dims" in msg
 
 
@@ -77,11 +77,11 @@ def test_rejects_head_mismatch_and_state_dtype():
     g = _fake([4, 4], _lib.MVB_F32)
     st = _fake([4, 4, 128, 128], _lib.MVB_F32)
     idx = _fake([4], _lib.MVB_I32)
-    rc, msg = _status("mvb_fused_recurrent_gdn", q, q, v, g, g, st, idx, v, ctypes.c_float(0.0), None)
+    rc, msg = _status("mvb_fused_recurrent_gdn", q, q, v, g, g, st, idx, v, ctypes.c_float(0.0), 0, None)
     assert rc == 1 and "multiple of Hk" in msg
     q = _fake([4, 2, 128])
     st16 = _fake([4, 4, 128, 128], _lib.MVB_BF16)
-    rc, msg = _status("mvb_fused_recurrent_gdn", q, q, v, g, g, st16, idx, v, ctypes.c_float(0.0), None)
+    rc, msg = _status("mvb_fused_recurrent_gdn", q, q, v, g, g, st16, idx, v, ctypes.c_float(0.0), 0, None)
     assert rc == 1 and "float32" in msg
 
 

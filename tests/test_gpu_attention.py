@@ -53,7 +53,7 @@ def test_varlen_prefill_c3_full_size_vs_torch_fp32():
             assert_close(o[a:b, h], ref, what=f"seq {s} head {h}")
 
 
-def _paged(lens_ctx, hkv, d, bs, seed, dtype=torch.bfloat16, extra_blocks=3):
+def _paged(lens_ctx, hkv, d, bs, seed, dtype=torch.bfloat16, extra_blocks=3, device="cpu"):
     g = torch.Generator().manual_seed(seed)
     nb_per = [max(1, (n + bs - 1) // bs) for n in lens_ctx]
     n_blocks = sum(nb_per) + extra_blocks
@@ -64,8 +64,13 @@ def _paged(lens_ctx, hkv, d, bs, seed, dtype=torch.bfloat16, extra_blocks=3):
     for s, nb in enumerate(nb_per):
         bt[s, :nb] = perm[o:o + nb].to(torch.int32)
         o += nb
-    kc = torch.randn(n_blocks, bs, hkv, d, generator=g).to(dtype)
-    vc = torch.randn(n_blocks, bs, hkv, d, generator=g).to(dtype)
+    if device == "cpu":
+        kc = torch.randn(n_blocks, bs, hkv, d, generator=g).to(dtype)
+        vc = torch.randn(n_blocks, bs, hkv, d, generator=g).to(dtype)
+    else:
+        gd = torch.Generator(device=device).manual_seed(seed)
+        kc = torch.randn(n_blocks, bs, hkv, d, generator=gd, device=device, dtype=dtype)
+        vc = torch.randn(n_blocks, bs, hkv, d, generator=gd, device=device, dtype=dtype)
     return kc, vc, bt
 
 
@@ -108,9 +113,9 @@ def test_paged_decode_small_block_and_unsplit():
 def test_paged_decode_c4_shapes_vs_torch_fp32():
     """Config-4 attention shapes: 128 seqs, ctx ~U[1024, 32768], Hq=16, Hkv=2, D=256, block 256."""
     ctx = W.seq_lengths(128, 1024, 32768, 4)
-    kc, vc, bt = _paged(ctx, 2, 256, 256, seed=4, extra_blocks=0)
+    kc, vc, bt = _paged(ctx, 2, 256, 256, seed=4, extra_blocks=0, device=dev)
     q = torch.randn(128, 16, 256).to(torch.bfloat16).to(dev)
-    kc, vc, bt = kc.to(dev), vc.to(dev), bt.to(dev)
+    bt = bt.to(dev)
     o = paged_flash_attention_decode(q, kc, vc, bt, torch.tensor(ctx, dtype=torch.int32, device=dev), 1 / 16, 256)
     for s in (0, 77, 127):
         n = ctx[s]

@@ -91,8 +91,8 @@ def test_chunk_continuation_equals_single_call():
     o1 = chunk_gated_delta_rule(a["q"], a["k"], a["v"], a["g"], a["beta"], a["state"], a["idx"], a["cu"])
     # second run: first 100 tokens of every sequence, then the rest
     cu = cpu["cu"].tolist()
-    first = [list(range(cu[s], cu[s] + 100)) for s in range(2)]
-    rest = [list(range(cu[s] + 100, cu[s + 1])) for s in range(2)]
+    first = [list(range(cu[s], min(cu[s] + 100, cu[s + 1]))) for s in range(2)]
+    rest = [list(range(cu[s] + len(first[s]), cu[s + 1])) for s in range(2)]
     outs = torch.empty_like(o1)
     for part in (first, rest):
         ids = torch.tensor(sum(part, []), device=dev)
@@ -150,3 +150,40 @@ def test_decode_c2_full_size_sampled():
                                     to_np(inp["beta"][pick]), st, idx)
     assert_close(o[pick], ref, what="o")
     assert state_rel_err(state[idx], st[idx]) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_chunk_fused_l2norm(dtype):
+    """use_qk_l2norm_in_kernel: unnormalised q/k in, same result as normalising first."""
+    lens = [70, 129]
+    cpu = _rand_gdn(lens, 2, 4, 128, 128, seed=21, dtype=dtype)
+    g_ = torch.Generator().manual_seed(3)
+    sc = 0.5 + 3 * torch.rand(sum(lens), 2, 1, generator=g_)
+    qr, kr = (cpu["q"].float() * sc).to(dtype), (cpu["k"].float() * sc.flip(0)).to(dtype)
+    gpu = _to(cpu, dev)
+    o = chunk_gated_delta_rule(qr.to(dev), kr.to(dev), gpu["v"], gpu["g"], gpu["beta"], gpu["state"], gpu["idx"],
+                               gpu["cu"], use_qk_l2norm_in_kernel=True)
+    qn = to_np(qr) / np.sqrt((to_np(qr) ** 2).sum(-1, keepdims=True) + 1e-6)
+    kn = to_np(kr) / np.sqrt((to_np(kr) ** 2).sum(-1, keepdims=True) + 1e-6)
+    st = cpu["state"].double().numpy()
+    ref = oracle.gdn.chunked(qn, kn, to_np(cpu["v"]), to_np(cpu["g"]), to_np(cpu["beta"]), st, cpu["idx"].numpy(),
+                             cpu["cu"].numpy(), 64)
+    assert_close(o, ref, what="o")
+    assert_state_close(gpu["state"], st)
+
+
+def test_decode_fused_l2norm():
+    S = 10
+    cpu = _rand_gdn([1] * S, 16, 32, 128, 128, seed=8, n_slots=12)
+    qr = (cpu["q"].float() * 3.0).to(torch.bfloat16)
+    kr = (cpu["k"].float() * 0.25).to(torch.bfloat16)
+    gpu = _to(cpu, dev)
+    o = fused_recurrent_gdn(qr.to(dev), kr.to(dev), gpu["v"], gpu["g"], gpu["beta"], gpu["state"], gpu["idx"],
+                            use_qk_l2norm_in_kernel=True)
+    qn = to_np(qr) / np.sqrt((to_np(qr) ** 2).sum(-1, keepdims=True) + 1e-6)
+    kn = to_np(kr) / np.sqrt((to_np(kr) ** 2).sum(-1, keepdims=True) + 1e-6)
+    st = cpu["state"].double().numpy()
+    ref = oracle.gdn.recurrent_step(qn, kn, to_np(cpu["v"]), to_np(cpu["g"]), to_np(cpu["beta"]), st,
+                                    cpu["idx"].numpy())
+    assert_close(o, ref, what="o")
+    assert state_rel_err(gpu["state"], st) < 1e-5
