@@ -85,11 +85,15 @@ int mvb_causal_conv1d_update(const mvb_tensor* x, const mvb_tensor* weight, mvb_
  * recurrent_state_indices[s] are read as the initial state and overwritten with the
  * final state; cu_seqlens [S+1]; o [T, Hv, V] (dtype of v).  scale <= 0 means K^-0.5.
  * use_qk_l2norm != 0 applies the layer's q/k L2 normalisation (x * rsqrt(sum x^2 + 1e-6),
- * m/layers/linear_attention.py:113-114) inside the kernel. */
+ * m/layers/linear_attention.py:113-114) inside the kernel.
+ * workspace: NULL, or >= 8 bytes of zero-initialised device memory used as a work counter
+ * (sequences are then scheduled dynamically, longest first); the kernel leaves it zeroed.
+ * Launches that share one workspace must be ordered (same stream). */
 int mvb_chunk_gated_delta_rule(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                                const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,
                                const mvb_tensor* recurrent_state_indices, const mvb_tensor* cu_seqlens,
-                               mvb_tensor* o, float scale, int use_qk_l2norm, void* stream);
+                               mvb_tensor* o, float scale, int use_qk_l2norm, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* Recurrent gated delta rule, one token per sequence (decode).  q,k [S, Hk, K];
  * v [S, Hv, V]; g, beta [S, Hv]; state [S_max, Hv, K, V] fp32 updated in place;
@@ -136,6 +140,20 @@ int mvb_store_kvcache(const mvb_tensor* k, const mvb_tensor* v, mvb_tensor* k_ca
  * x, gate, out [N, D]; weight [D]. */
 int mvb_rmsnorm_gated(const mvb_tensor* x, const mvb_tensor* gate, const mvb_tensor* weight, float eps,
                       mvb_tensor* out, void* stream);
+
+/* Diagnostics. */
+
+/* Reads and clears the kernels' device error word: 0 = no error; 1 = a bounded wait on a
+ * tensor-core completion barrier gave up (the kernel abandoned its work and freed its
+ * tensor memory).  Synchronises with the device. */
+int mvb_device_status(int* status);
+
+/* Tensor-core self-test: D[128, n] = A B1 + (negate ? -1 : 1) A B2 on one CTA with
+ * fp16 operands staged in the 128-byte-swizzle K-major (a_mn/b_mn = 0) or MN-major (= 1)
+ * layouts the kernels use.  Storage: A [128][k] (K-major) or [k][128]; B [n][k] or [k][n];
+ * D [128][n] fp32.  n, k in {64, 128}. */
+int mvb_selftest_umma(const void* a, const void* b1, const void* b2, float* d, int n, int k, int a_mn, int b_mn,
+                      int negate, void* stream);
 
 #ifdef __cplusplus
 }

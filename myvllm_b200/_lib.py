@@ -42,7 +42,7 @@ SIGNATURES = {
     "mvb_causal_conv1d_fn": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, ctypes.c_int, _P]),
     "mvb_causal_conv1d_update": (ctypes.c_int, [_T, _T, _T, _T, _T, ctypes.c_int, _P]),
     "mvb_chunk_gated_delta_rule": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int,
-                                                  _P]),
+                                                  _P, ctypes.c_size_t, _P]),
     "mvb_fused_recurrent_gdn": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int, _P]),
     "mvb_flash_attention_prefill": (ctypes.c_int, [_T, _T, _T, _T, ctypes.c_float, ctypes.c_int, ctypes.c_int,
                                                    ctypes.c_int, ctypes.c_int, ctypes.c_int, _T, _P]),
@@ -52,6 +52,9 @@ SIGNATURES = {
     "mvb_paged_attention_prefill": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int, _T, _P]),
     "mvb_store_kvcache": (ctypes.c_int, [_T, _T, _T, _T, _T, _P]),
     "mvb_rmsnorm_gated": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, _T, _P]),
+    "mvb_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "mvb_selftest_umma": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_int, _P]),
 }
 
 _lib = None
@@ -126,12 +129,20 @@ def call(op: str, fn_name: str, *args) -> None:
 _workspaces: dict = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A per-device scratch buffer, grown on demand and reused across calls on the
-    current stream (kernels on one stream are ordered, so reuse is safe there)."""
-    key = (device.type, device.index)
+def workspace(device: torch.device, nbytes: int, tag: str = "scratch") -> torch.Tensor:
+    """A per-device, per-op scratch buffer, grown on demand, zero-initialised and reused
+    across calls (kernels on one stream are ordered, so reuse is safe there; ops running
+    concurrently on different streams must not share one)."""
+    key = (device.type, device.index, tag)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf
+
+
+def device_status() -> int:
+    """Reads and clears the kernels' device error word (0 = ok); synchronises."""
+    v = ctypes.c_int(0)
+    check("device_status", load().mvb_device_status(ctypes.byref(v)))
+    return v.value

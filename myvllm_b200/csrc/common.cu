@@ -1,4 +1,6 @@
 // Status plumbing shared by every entry point of libmyvllm_b200.
+#include <vector>
+
 #include "common.cuh"
 
 namespace mvb {
@@ -21,6 +23,24 @@ int check_tensor(const mvb_tensor* t, const char* op, const char* name, int ndim
   return MVB_OK;
 }
 
+static std::vector<StatusReader>& status_readers() {
+  static std::vector<StatusReader> v;
+  return v;
+}
+
+void register_status_reader(StatusReader f) { status_readers().push_back(f); }
+
+int read_all_status(int* out) {
+  int worst = 0;
+  for (StatusReader f : status_readers()) {
+    int s = 0;
+    if (f(&s) != 0) return -1;
+    worst = s > worst ? s : worst;
+  }
+  *out = worst;
+  return 0;
+}
+
 int num_sms() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -34,5 +54,11 @@ extern "C" {
 int mvb_version(void) { return 100; }
 
 const char* mvb_last_error(void) { return mvb::g_last_error; }
+
+int mvb_device_status(int* status) {
+  if (status == nullptr) MVB_FAIL(MVB_ERR_ARG, "device_status: null pointer");
+  if (mvb::read_all_status(status) != 0) MVB_FAIL(MVB_ERR_CUDA, "device_status: reading the error words failed");
+  return MVB_OK;
+}
 
 }  // extern "C"

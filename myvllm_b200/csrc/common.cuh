@@ -62,6 +62,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int num_sms();
 
+// Host readers of the per-translation-unit device error words (see tcgen05.cuh).
+using StatusReader = int (*)(int*);
+void register_status_reader(StatusReader f);
+
 // ------------------------------------------------------------- dtype math ----
 template <typename T>
 __device__ __forceinline__ float to_f32(T x);

@@ -11,9 +11,12 @@
 // ceil(T/TILE) + S and surplus CTAs exit).  The tile holding a sequence's first token
 // is the only reader of its old conv state; it also writes the new state (reading the
 // tail of x directly), so there is no cross-CTA race on conv_state.
-// Each thread owns VEC=8 contiguous channels (one 16-byte access per row) and walks
-// the tile's tokens with a register sliding window; rows are loaded 8 at a time to
-// keep several 16-byte loads in flight per thread.
+// Fast path (16-bit data, contiguous 16-byte aligned rows): a CTA stages its tile of
+// TILE + W - 1 rows x 1024 channels (history rows from x or, at a sequence start, from
+// conv_state) into shared memory with 16-byte cp.async -- every load of the tile in
+// flight at once -- then each thread runs a register sliding window over 8 channels.
+// Generic path (fp32, strided or unaligned): one thread per VEC channels reading rows
+// directly.
 #include "common.cuh"
 
 namespace mvb {
@@ -191,6 +194,76 @@ __global__ void __launch_bounds__(128) conv1d_fwd_kernel(ConvParams p) {
   }
 }
 
+constexpr int kSmemTile = 16;  // tokens per CTA tile on the fast path
+
+template <typename T, typename TW, int W>
+__global__ void __launch_bounds__(128) conv1d_fwd_smem_kernel(ConvParams p) {
+  constexpr int ROWS = kSmemTile + W - 1;
+  __shared__ __align__(16) uint4 tile[ROWS][128];  // [row][16-byte channel group]
+  int seq, pos0;
+  if (!find_tile(p.cu, p.n_seqs, kSmemTile, blockIdx.x, seq, pos0)) return;
+  const int tid = threadIdx.x;
+  const int c0 = (blockIdx.y * 128 + tid) * 8;
+  const bool ok_c = c0 < p.dim;
+  const int start = p.cu[seq];
+  const int L = p.cu[seq + 1] - start;
+  const int pend = min(L, pos0 + kSmemTile);
+  const T* x = static_cast<const T*>(p.x);
+  T* st = static_cast<T*>(p.state) + (int64_t)p.idx[seq] * p.ss_n;
+  // rows: tile row r holds xp[pos0 + r]; xp index e < W-1 is state row e, else x[start + e - (W-1)]
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    const int e = pos0 + r;
+    const bool in = ok_c && (e < W - 1 || e - (W - 1) < L);
+    const T* src = e < W - 1 ? st + e * p.ss_t + c0 : x + (int64_t)(start + e - (W - 1)) * p.sx_t + c0;
+    cp_async16(&tile[r][tid], in ? src : x, in);
+  }
+  cp_async_commit();
+  float w[W][8];
+  const TW* wp = static_cast<const TW*>(p.w);
+#pragma unroll
+  for (int j = 0; j < W; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[j][i] = ok_c ? to_f32<TW>(wp[(int64_t)(c0 + i) * p.sw_c + j * p.sw_j]) : 0.f;
+  cp_async_wait<0>();
+  if (!ok_c) return;  // no barrier follows: each thread reads only the column it staged
+
+  // new conv state (only the tile holding position 0 reads and writes conv_state)
+  if (pos0 == 0) {
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      const int e = L + j;  // xp index of new state row j
+      uint4 val;
+      if (e < ROWS) val = tile[e][tid];
+      else val = *reinterpret_cast<const uint4*>(x + (int64_t)(start + e - (W - 1)) * p.sx_t + c0);
+      *reinterpret_cast<uint4*>(st + j * p.ss_t + c0) = val;
+    }
+  }
+  float win[W][8];
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) unpack8<T>(tile[j][tid], win[j]);
+  T* out = static_cast<T*>(p.out);
+#pragma unroll
+  for (int t = 0; t < kSmemTile; ++t) {
+    if (pos0 + t < pend) {
+      unpack8<T>(tile[t + W - 1][tid], win[W - 1]);
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < W; ++j) a += w[j][i] * win[j][i];
+        acc[i] = p.silu ? __fdividef(a, 1.f + __expf(-a)) : a;
+      }
+      *reinterpret_cast<uint4*>(out + (int64_t)(start + pos0 + t) * p.so_t + c0) = pack8<T>(acc);
+#pragma unroll
+      for (int j = 0; j < W - 1; ++j)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) win[j][i] = win[j + 1][i];
+    }
+  }
+}
+
 // Decode: one token per sequence; grid (dim / (128 VEC), S).
 template <typename T, typename TW, int VEC, int W>
 __global__ void __launch_bounds__(128) conv1d_update_kernel(ConvParams p) {
@@ -241,9 +314,13 @@ void launch_w(bool prefill, bool vec8, const ConvParams& p, int64_t T_tokens, cu
   const int VEC = vec8 ? 8 : 1;
   const int chan_blocks = (p.dim + 128 * VEC - 1) / (128 * VEC);
   if (prefill) {
-    dim3 grid((unsigned)((T_tokens + p.tile - 1) / p.tile + p.n_seqs), chan_blocks);
-    if (vec8) conv1d_fwd_kernel<T, TW, 8, W><<<grid, 128, 0, st>>>(p);
-    else conv1d_fwd_kernel<T, TW, 1, W><<<grid, 128, 0, st>>>(p);
+    if (vec8) {
+      dim3 grid((unsigned)((T_tokens + kSmemTile - 1) / kSmemTile + p.n_seqs), chan_blocks);
+      conv1d_fwd_smem_kernel<T, TW, W><<<grid, 128, 0, st>>>(p);
+    } else {
+      dim3 grid((unsigned)((T_tokens + p.tile - 1) / p.tile + p.n_seqs), chan_blocks);
+      conv1d_fwd_kernel<T, TW, 1, W><<<grid, 128, 0, st>>>(p);
+    }
   } else {
     dim3 grid(chan_blocks, p.n_seqs);
     if (vec8) conv1d_update_kernel<T, TW, 8, W><<<grid, 128, 0, st>>>(p);

@@ -31,13 +31,21 @@ struct RecParams {
   int64_t sq_t, sq_h, sq_d, sk_t, sk_h, sk_d, sv_t, sv_h, sv_d, so_t, so_h, so_d;
   int64_t sg_t, sg_h, sb_t, sb_h;
   int64_t ss_n, ss_h, ss_k;  // state strides (V stride must be 1)
-  int hk, hv, vdim, l2norm;
+  int hk, hv, vdim, l2norm, g_dtype, b_dtype;
   float scale;
 };
 
+// g and beta may each be fp32 or the activation dtype (the reference layer makes g fp32
+// and beta bf16, m/layers/linear_attention.py:89-90).
+__device__ __forceinline__ float load_gate(const void* p, int64_t i, int dtype) {
+  if (dtype == MVB_F32) return static_cast<const float*>(p)[i];
+  if (dtype == MVB_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+
 constexpr int kThreads = 128;
 
-template <typename T, typename TG, int K, int VS>
+template <typename T, int K, int VS>
 __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(RecParams p) {
   constexpr int CG = VS / 4;           // float4 column groups per slice
   constexpr int RP = kThreads / CG;    // rows per pass
@@ -79,8 +87,6 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(RecParams p) {
   const T* qp = static_cast<const T*>(p.q);
   const T* kp = static_cast<const T*>(p.k);
   const T* vp = static_cast<const T*>(p.v);
-  const TG* gp = static_cast<const TG*>(p.g);
-  const TG* bp = static_cast<const TG*>(p.beta);
   T* op = static_cast<T*>(p.o);
 
   for (int t = t_begin; t < t_end; ++t) {
@@ -93,8 +99,8 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(RecParams p) {
       sv[i] = vv < p.vdim ? to_f32<T>(vp[t * p.sv_t + h * p.sv_h + vv * p.sv_d]) : 0.f;
     }
     if (tid == 0) {
-      s_gb[0] = expf(to_f32<TG>(gp[t * p.sg_t + h * p.sg_h]));
-      s_gb[1] = to_f32<TG>(bp[t * p.sb_t + h * p.sb_h]);
+      s_gb[0] = expf(load_gate(p.g, (int64_t)t * p.sg_t + h * p.sg_h, p.g_dtype));
+      s_gb[1] = load_gate(p.beta, (int64_t)t * p.sb_t + h * p.sb_h, p.b_dtype);
     }
     __syncthreads();
     if (p.l2norm) {
@@ -185,20 +191,20 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(RecParams p) {
   }
 }
 
-template <typename T, typename TG, int K>
+template <typename T, int K>
 void launch_rec(const RecParams& p, int n_seqs, cudaStream_t st) {
   constexpr int VS = 64;
   dim3 grid((p.vdim + VS - 1) / VS, p.hv, n_seqs);
-  gdn_recurrent_kernel<T, TG, K, VS><<<grid, kThreads, 0, st>>>(p);
+  gdn_recurrent_kernel<T, K, VS><<<grid, kThreads, 0, st>>>(p);
 }
 
-template <typename T, typename TG>
+template <typename T>
 int dispatch_k(const RecParams& p, int kdim, int n_seqs, cudaStream_t st) {
   switch (kdim) {
-    case 32: launch_rec<T, TG, 32>(p, n_seqs, st); break;
-    case 64: launch_rec<T, TG, 64>(p, n_seqs, st); break;
-    case 128: launch_rec<T, TG, 128>(p, n_seqs, st); break;
-    case 256: launch_rec<T, TG, 256>(p, n_seqs, st); break;
+    case 32: launch_rec<T, 32>(p, n_seqs, st); break;
+    case 64: launch_rec<T, 64>(p, n_seqs, st); break;
+    case 128: launch_rec<T, 128>(p, n_seqs, st); break;
+    case 256: launch_rec<T, 256>(p, n_seqs, st); break;
     default: MVB_FAIL(MVB_ERR_UNSUPPORTED, "gated delta rule: K=%d not in {32,64,128,256}", kdim);
   }
   return MVB_OK;
@@ -232,8 +238,8 @@ int check_gdn(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
   MVB_CHECK_ARG(idx->dtype == MVB_I32, "%s: recurrent_state_indices must be int32", op);
   MVB_CHECK_ARG(q->dtype == k->dtype && q->dtype == v->dtype && o->dtype == v->dtype && is_float_dtype(q->dtype),
                 "%s: q/k/v/o must share one float dtype", op);
-  MVB_CHECK_ARG(g->dtype == beta->dtype && (g->dtype == MVB_F32 || g->dtype == q->dtype),
-                "%s: g/beta must be float32 or the dtype of q", op);
+  MVB_CHECK_ARG((g->dtype == MVB_F32 || g->dtype == q->dtype) && (beta->dtype == MVB_F32 || beta->dtype == q->dtype),
+                "%s: g and beta must each be float32 or the dtype of q", op);
   int64_t n_seqs = T;
   if (cu != nullptr) {
     if ((rc = check_tensor(cu, op, "cu_seqlens", 1))) return rc;
@@ -272,12 +278,13 @@ int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, cons
   p.hk = (int)hk; p.hv = (int)hv; p.vdim = (int)vd; p.l2norm = l2norm ? 1 : 0;
   p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)kd);
 
+  p.g_dtype = g->dtype;
+  p.b_dtype = beta->dtype;
   int r = MVB_OK;
-  const bool g32 = g->dtype == MVB_F32;
   switch (q->dtype) {
-    case MVB_F32: r = g32 ? dispatch_k<float, float>(p, kd, n_seqs, st) : dispatch_k<float, __nv_bfloat16>(p, kd, n_seqs, st); break;
-    case MVB_BF16: r = g32 ? dispatch_k<__nv_bfloat16, float>(p, kd, n_seqs, st) : dispatch_k<__nv_bfloat16, __nv_bfloat16>(p, kd, n_seqs, st); break;
-    case MVB_F16: r = g32 ? dispatch_k<__half, float>(p, kd, n_seqs, st) : dispatch_k<__half, __half>(p, kd, n_seqs, st); break;
+    case MVB_F32: r = dispatch_k<float>(p, kd, n_seqs, st); break;
+    case MVB_BF16: r = dispatch_k<__nv_bfloat16>(p, kd, n_seqs, st); break;
+    case MVB_F16: r = dispatch_k<__half>(p, kd, n_seqs, st); break;
   }
   if (r != MVB_OK) return r;
   MVB_CHECK_LAUNCH(op);

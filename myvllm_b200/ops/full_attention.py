@@ -53,7 +53,7 @@ def paged_flash_attention_decode(
     o = torch.empty(seq_cnt, num_q_heads, v_head_dim, dtype=q.dtype, device=q.device)
     bound = int(max_context_len) if max_context_len else int(block_tables.shape[1]) * int(block_size)
     nbytes = _lib.load().mvb_paged_attention_decode_workspace_size(seq_cnt, num_kv_heads, v_head_dim, bound)
-    ws = _lib.workspace(q.device, nbytes) if nbytes else None
+    ws = _lib.workspace(q.device, nbytes, tag="paged_decode") if nbytes else None
     _lib.call("paged_flash_attention_decode", "mvb_paged_attention_decode", _lib.desc(q), _lib.desc(k_cache),
               _lib.desc(v_cache), _lib.desc(_i32(block_tables)), _lib.desc(_i32(context_lens)), float(scale),
               int(block_size), bound, _lib.desc(o), ws.data_ptr() if ws is not None else None,

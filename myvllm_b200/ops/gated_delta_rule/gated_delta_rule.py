@@ -51,9 +51,11 @@ def chunk_gated_delta_rule(
     idx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
     cu = cu_seqlens if cu_seqlens.dtype == torch.int32 else cu_seqlens.int()
     o = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    ws = _lib.workspace(q.device, 8, tag="gdn_chunk")  # work counter of the dynamic scheduler
     _lib.call("chunk_gated_delta_rule", "mvb_chunk_gated_delta_rule", _lib.desc(q), _lib.desc(k), _lib.desc(v),
               _lib.desc(g), _lib.desc(beta), _lib.desc(recurrent_state), _lib.desc(idx), _lib.desc(cu),
-              _lib.desc(o), float(k.shape[-1] ** -0.5), int(use_qk_l2norm_in_kernel), _lib.stream_of(q))
+              _lib.desc(o), float(k.shape[-1] ** -0.5), int(use_qk_l2norm_in_kernel), ws.data_ptr(), ws.numel(),
+              _lib.stream_of(q))
     return o
 
 

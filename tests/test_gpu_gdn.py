@@ -187,3 +187,24 @@ def test_decode_fused_l2norm():
                                     cpu["idx"].numpy())
     assert_close(o, ref, what="o")
     assert state_rel_err(gpu["state"], st) < 1e-5
+
+
+def test_chunk_mixed_gate_dtypes():
+    """The reference layer hands over g in fp32 and beta in the activation dtype."""
+    lens = [100, 64]
+    cpu = _rand_gdn(lens, 2, 4, 128, 128, seed=31)
+    cpu["beta"] = cpu["beta"].to(torch.bfloat16)
+    gpu = _to(cpu, dev)
+    o = chunk_gated_delta_rule(gpu["q"], gpu["k"], gpu["v"], gpu["g"], gpu["beta"], gpu["state"], gpu["idx"],
+                               gpu["cu"])
+    st = cpu["state"].double().numpy()
+    ref = oracle.gdn.chunked(to_np(cpu["q"]), to_np(cpu["k"]), to_np(cpu["v"]), to_np(cpu["g"]), to_np(cpu["beta"]),
+                             st, cpu["idx"].numpy(), cpu["cu"].numpy(), 64)
+    assert_close(o, ref, what="o")
+    assert_state_close(gpu["state"], st)
+
+
+def test_chunk_no_device_timeouts():
+    from myvllm_b200 import _lib
+
+    assert _lib.device_status() == 0
