@@ -123,6 +123,17 @@ int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor* k_cache, c
                                int block_size, int64_t max_context_len, mvb_tensor* o, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of mvb_paged_attention_decode (no counterpart in the reference).
+ * For callers that may not allocate device memory when they decode: the split-KV partial
+ * results go to a fixed 16 MiB array in the library's device image instead of a caller
+ * workspace.  It splits as far as that array allows and returns MVB_ERR_UNSUPPORTED when
+ * n_seqs * num_kv_heads * (head_dim + 1) * 128 bytes (two splits) exceed 16 MiB.
+ * The first call on each device looks up the array's device address (make it before any
+ * stream capture).  All calls share the array: calls that overlap on the GPU race. */
+int mvb_paged_attention_decode_noalloc(const mvb_tensor* q, const mvb_tensor* k_cache, const mvb_tensor* v_cache,
+                                       const mvb_tensor* block_tables, const mvb_tensor* context_lens, float scale,
+                                       int block_size, int64_t max_context_len, mvb_tensor* o, void* stream);
+
 /* Prefill continuing from a paged cache: the L_s queries of sequence s sit at positions
  * context_lens[s] - L_s + i and attend causally to cached tokens [0, context_lens[s]).
  * q [T, Hq, D]; cu_seqlens [S+1]; other arguments as in mvb_paged_attention_decode. */

@@ -12,6 +12,8 @@
 // the padded rows are never written).  Long contexts are split across CTAs
 // (flash-decoding); split results (normalised O and log2-sum-exp) go to the caller's
 // workspace and a second kernel merges them.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mvb {
@@ -415,4 +417,72 @@ extern "C" int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor*
   return mvb::run_paged_decode("paged_attention_decode", q, k_cache, v_cache, block_tables, context_lens, scale,
                                block_size, max_context_len, o, workspace, workspace_bytes, mvb::kMaxSplits,
                                static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free paged decode.
+//
+// Some callers cannot allocate device memory at the point where they decode: a host
+// runtime that owns all device memory and hands a plugin only the tensors it needs, or a
+// latency-critical step where the allocator may synchronise the device.  This entry point
+// needs no workspace: the split-KV partial results go to a fixed array that is part of the
+// library's device image (every GPU that loads the library holds these 16 MiB until the
+// process exits).  Nothing in the array has to start at zero: each call writes every
+// partial it later reads.  All calls share the one array, so calls whose kernels overlap on
+// the GPU (e.g. on two streams) race; issue them in order.
+namespace mvb {
+namespace {
+
+constexpr size_t kDecodeScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) char g_decode_scratch[kDecodeScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_decode_scratch_mu;
+void* g_decode_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_decode_scratch on the current device.  The first call on a device
+// looks it up (cudaGetSymbolAddress); later calls reuse it.
+int decode_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) MVB_FAIL(MVB_ERR_CUDA, "paged_attention_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) MVB_FAIL(MVB_ERR_UNSUPPORTED, "paged_attention_decode_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_decode_scratch_mu);
+  if (g_decode_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      MVB_FAIL(MVB_ERR_CUDA, "paged_attention_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_decode_scratch_addr[dev] = p;
+  }
+  *out = g_decode_scratch_addr[dev];
+  return MVB_OK;
+}
+
+}  // namespace
+}  // namespace mvb
+
+extern "C" int mvb_paged_attention_decode_noalloc(const mvb_tensor* q, const mvb_tensor* k_cache,
+                                                  const mvb_tensor* v_cache, const mvb_tensor* block_tables,
+                                                  const mvb_tensor* context_lens, float scale, int block_size,
+                                                  int64_t max_context_len, mvb_tensor* o, void* stream) {
+  using namespace mvb;
+  const char* op = "paged_attention_decode_noalloc";
+  int rc;
+  if ((rc = check_tensor(q, op, "q", 3)) || (rc = check_tensor(k_cache, op, "k_cache", 4)) ||
+      (rc = check_tensor(v_cache, op, "v_cache", 4)))
+    return rc;
+  const int64_t S = q->shape[0], hkv = k_cache->shape[2], dv = v_cache->shape[3];
+  const size_t per_split = (size_t)(S > 0 ? S : 1) * (size_t)(hkv > 0 ? hkv : 1) * 16 * (size_t)(dv + 1) * sizeof(float);
+  const size_t fit = kDecodeScratchBytes / per_split;
+  if (fit < 2)
+    MVB_FAIL(MVB_ERR_UNSUPPORTED,
+             "%s: %lld sequences x %lld kv heads x head dim %lld need %zu bytes of split scratch for 2 splits; "
+             "the built-in scratch holds %zu bytes (use mvb_paged_attention_decode with a workspace)",
+             op, (long long)S, (long long)hkv, (long long)dv, 2 * per_split, kDecodeScratchBytes);
+  void* scratch = nullptr;
+  if ((rc = decode_scratch_address(&scratch))) return rc;
+  const int64_t max_splits = fit < (size_t)kMaxSplits ? (int64_t)fit : (int64_t)kMaxSplits;
+  return run_paged_decode(op, q, k_cache, v_cache, block_tables, context_lens, scale, block_size, max_context_len, o,
+                          scratch, kDecodeScratchBytes, max_splits, static_cast<cudaStream_t>(stream));
 }
