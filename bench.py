@@ -370,6 +370,136 @@ def run_c3(args, rank, world, device):
             "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
 
 
+# ----------------------------------------------------------------------------- c4 ----
+def run_c4(args, rank, world, device):
+    """Config 4: one decode step of a 48-layer hybrid stack (36 GDN + 12 gated full
+    attention, hidden 2048, pre-norm + mixer + residual; no MLP/MoE), 128 sequences with
+    context ~U[1024, 32768] in a paged bf16 KV cache (block 256) and fp32 GDN states.
+    Heads are tensor-parallel over the ranks with an NCCL all-reduce after every output
+    projection; KV heads are replicated past TP 2."""
+    from myvllm_b200 import workloads as W
+    from myvllm_b200.cache.linear_attention_cache import LinearAttentionCache, PagedKVCache
+    from myvllm_b200.layers.full_attention import GatedAttention
+    from myvllm_b200.layers.linear_attention import GatedDeltaNet
+    from myvllm_b200.layers.norm import RMSNorm
+    from myvllm_b200.layers.rotary_embedding import RotaryEmbedding
+    from myvllm_b200.utils.context import set_context
+
+    torch.manual_seed(1234)  # identical weights on every rank (each loads its shard)
+    S, hidden, n_layers, bs = 128, 2048, 48, 256
+    kinds = ["full" if (i + 1) % 4 == 0 else "gdn" for i in range(n_layers)]
+    layers = []
+    for kind in kinds:
+        mixer = GatedDeltaNet(hidden, 16, 32, 128, 128, 4) if kind == "gdn" else \
+            GatedAttention(hidden, 256, 16, 256, 2, False, 1e-6)
+        for name, prm in mixer.named_parameters():
+            if not (name.endswith("A_log") or name.endswith("dt_bias") or "norm" in name):
+                prm.data.normal_(0.0, 0.02)
+        mixer = mixer.to(device, torch.bfloat16)
+        if kind == "gdn":
+            mixer.A_log.data = mixer.A_log.data.float()
+            mixer.dt_bias.data = mixer.dt_bias.data.float()
+        layers.append((RMSNorm((hidden,), 1e-6, True).to(device, torch.bfloat16), mixer))
+    gdn = [m for k, (_, m) in zip(kinds, layers) if k == "gdn"]
+    fa = [m for k, (_, m) in zip(kinds, layers) if k == "full"]
+    lac = LinearAttentionCache(len(gdn), S, 4, 128, 128, gdn[0].num_k_heads, gdn[0].num_v_heads, torch.bfloat16,
+                               device)
+    lac.recurrent_cache.normal_(0.0, 0.1)
+    lac.conv_cache.normal_(0.0, 1.0)
+    for i, m in enumerate(gdn):
+        m.conv_state, m.recurrent_state = lac.layer_states(i)
+    ctx_lens = W.seq_lengths(S, 1024, 32768, 4)
+    steps_total = args.warmup + args.steps + 4
+    n_blocks = sum((c + steps_total + bs - 1) // bs for c in ctx_lens)
+    kv = PagedKVCache(len(fa), n_blocks, bs, fa[0].num_kv_heads, 256, torch.bfloat16, device)
+    for i in range(len(fa)):  # fill the caches layer by layer (bounded temporaries)
+        kv.k[i].normal_()
+        kv.v[i].normal_()
+    for i, m in enumerate(fa):
+        m.k_cache, m.v_cache = kv.layer_caches(i)
+    seq_ids = list(range(S))
+    for s, c in enumerate(ctx_lens):
+        kv.append(s, c)
+    idx = torch.arange(S, dtype=torch.int32, device=device)
+    rope = RotaryEmbedding(64, 10_000_000.0).to(device)
+    meta = []  # per-step metadata, built before timing
+    for step in range(steps_total):
+        for s in seq_ids:
+            kv.append(s, 1)
+        bt, cl, slots = kv.metadata(seq_ids, [1] * S)
+        cos, sin = rope.cos_sin((cl - 1).long())
+        meta.append((bt, cl, slots, cos, sin))
+    g_ = torch.Generator(device=device).manual_seed(7)
+    x0 = torch.randn(S, hidden, generator=g_, device=device, dtype=torch.bfloat16)
+
+    def step(i, x):
+        bt, cl, slots, cos, sin = meta[i]
+        set_context(False, slot_mapping=slots, context_lens=cl, block_tables=bt, block_size=bs)
+        for (norm, mixer), kind in zip(layers, kinds):
+            h = norm(x)
+            if kind == "gdn":
+                h = mixer(h, None, idx, idx, False)
+            else:
+                h = mixer(h, cos, sin)
+            x = x + h
+        return x
+
+    with torch.no_grad():
+        for i in range(args.warmup):
+            step(i, x0)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        clk = ClockSampler(device.index or 0).__enter__()
+        time.sleep(0.5)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk.mark_start()
+        s0.record()
+        for i in range(args.steps):
+            step(args.warmup + i, x0)
+        s1.record()
+        torch.cuda.synchronize()
+        clk.mark_stop()
+        clk.__exit__()
+        ms = s0.elapsed_time(s1) / args.steps
+        # end to end: hidden states in from pinned host memory, out to pinned host memory
+        xh = x0.cpu().pin_memory()
+        oh = torch.empty_like(xh).pin_memory()
+        xd = torch.empty_like(x0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(3):
+            xd.copy_(xh, non_blocking=True)
+            oh.copy_(step(args.warmup + args.steps + i % 4, xd), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / 3
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = t[0].item(), t[1].item()
+    if rank != 0:
+        return None
+    hkv_rank = fa[0].num_kv_heads
+    kv_bytes = sum(ctx_lens) * len(fa) * hkv_rank * 256 * 2 * 2
+    state_bytes = 2 * lac.recurrent_cache.numel() * 4 + 2 * lac.conv_cache.numel() * 2
+    w_bytes = sum(p.numel() * p.element_size() for _, m in layers for p in m.parameters())
+    step_bytes = kv_bytes + state_bytes + w_bytes
+    pk, src = peaks()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    return {"metric": "decode us/step (48-layer hybrid stack, 128 seqs)", "value": ms * 1e3, "unit": "us",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "c4: 36 GDN + 12 gated-attention layers, hidden 2048, 128 seqs, ctx ~U[1024,32768]",
+                       "parallelism": f"tp{world}", "l2": "KV and states far larger than L2"},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step (per rank)", "achieved": gbs,
+                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": src,
+                         "bytes_per_step_rank0": step_bytes, "traffic": None},
+            "e2e": {"value": e2e_ms * 1e3, "unit": "us", "h2d_bytes_per_step": xh.numel() * 2,
+                    "d2h_bytes_per_step": oh.numel() * 2},
+            "gpu_launches": None, "clocks": clk.summary()}
+
+
 # ------------------------------------------------------------------------ reference ----
 def run_reference(args):
     """The CPU restatement of the reference path on this host's cores, on the c1 metric."""
@@ -401,7 +531,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
-    ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3"])
+    ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3", "c4"])
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -422,7 +552,7 @@ def main():
     from myvllm_b200 import _lib
 
     _lib.load()  # fail loudly if the library is missing
-    fn = {"c1": run_c1, "c2": run_c2, "c3": run_c3}[args.config]
+    fn = {"c1": run_c1, "c2": run_c2, "c3": run_c3, "c4": run_c4}[args.config]
     line = fn(args, rank, world, device)
     if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)

@@ -62,6 +62,20 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int num_sms();
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device): the
+// attribute belongs to the device context, so a process driving several GPUs needs it on
+// each.  `mask` is a per-kernel bit set of devices already configured.
+template <typename F>
+inline void ensure_smem_attr(F* func, int bytes, unsigned long long& mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(mask & bit)) {
+    cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    mask |= bit;
+  }
+}
+
 // Host readers of the per-translation-unit device error words (see tcgen05.cuh).
 using StatusReader = int (*)(int*);
 void register_status_reader(StatusReader f);

@@ -260,11 +260,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) flash_prefill_kernel(FaParams 
 template <typename T, int D, bool PAGED>
 void launch_fa(const FaParams& p, int64_t T_tokens, cudaStream_t st) {
   constexpr int smem = BM * D * 2 + 2 * 2 * BN * D * 2;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(flash_prefill_kernel<T, D, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  static unsigned long long attr_mask = 0;
+  ensure_smem_attr(flash_prefill_kernel<T, D, PAGED>, smem, attr_mask);
   dim3 grid(p.hq, (unsigned)((T_tokens + BM - 1) / BM + p.n_seqs));
   flash_prefill_kernel<T, D, PAGED><<<grid, kWarps * 32, smem, st>>>(p);
 }

@@ -691,19 +691,12 @@ int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* 
   const int chains = (int)(n_seqs * p.hv);
   const int grid = chains < num_sms() ? chains : num_sms();
   if (q->dtype == MVB_BF16) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(gdn_chunk_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           SMEM_BYTES);
-      attr = true;
-    }
+    static unsigned long long attr_mask = 0;
+    ensure_smem_attr(gdn_chunk_tc_kernel<__nv_bfloat16>, SMEM_BYTES, attr_mask);
     gdn_chunk_tc_kernel<__nv_bfloat16><<<grid, kThreads, SMEM_BYTES, st>>>(p);
   } else {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(gdn_chunk_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-      attr = true;
-    }
+    static unsigned long long attr_mask = 0;
+    ensure_smem_attr(gdn_chunk_tc_kernel<__half>, SMEM_BYTES, attr_mask);
     gdn_chunk_tc_kernel<__half><<<grid, kThreads, SMEM_BYTES, st>>>(p);
   }
   MVB_CHECK_LAUNCH("chunk_gated_delta_rule");

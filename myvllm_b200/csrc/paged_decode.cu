@@ -311,11 +311,8 @@ size_t decode_workspace_bytes(int64_t n_seqs, int64_t hkv, int64_t dv, int n_spl
 template <typename T, int D>
 int launch_decode(DecodeParams& p, int64_t n_seqs, cudaStream_t st) {
   const int smem = DecodeSmem<D>::kBytes;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(paged_decode_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr_set = true;
-  }
+  static unsigned long long attr_mask = 0;
+  ensure_smem_attr(paged_decode_kernel<T, D>, smem, attr_mask);
   dim3 grid(p.n_splits, p.hkv, (unsigned)n_seqs);
   paged_decode_kernel<T, D><<<grid, kWarps * 32, smem, st>>>(p);
   if (p.n_splits > 1) {

@@ -1,0 +1,87 @@
+"""Gated full-attention layer (drop-in for ``myvllm.layers.full_attention.GatedAttention``).
+
+Constructor and ``forward(x, rotary_pos_emb_cos, rotary_pos_emb_sin)`` as in the reference
+(``m/layers/full_attention.py:10-64``), which stops after RoPE and returns an empty tensor.
+Completed here with the Qwen3.5 gated attention the config describes
+(``attn_output_gate``, partial rotary):
+
+    q, gate = q_proj(x)           (per head: [q | gate], GatedQParallelLinear)
+    q, k    = q_norm(q), k_norm(k_proj(x));  v = v_proj(x)
+    q, k    = RoPE on the first 2 * cos.shape[-1] dims
+    store_kvcache(k, v) at context.slot_mapping            (when a cache is attached)
+    o       = varlen causal prefill | paged prefill | paged decode   (from the Context)
+    out     = o_proj(o * sigmoid(gate))                    (all_reduce at TP > 1)
+
+Attention metadata comes from ``myvllm_b200.utils.context`` (the reference sketches the
+same fields there).  KV heads are split across ranks at TP <= Hkv and replicated at larger
+TP (the reference asserts ``num_kv_heads % tp == 0``).  ``k_cache``/``v_cache`` are
+attributes the caller points at its paged cache ``[n_blocks, block_size, Hkv_rank, D]``.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from ..ops.full_attention import flash_attention_prefill, paged_flash_attention_decode, paged_flash_attention_prefill
+from ..ops.kv_cache import store_kvcache
+from ..utils.context import get_context
+from .linear import GatedQParallelLinear, KVParallelLinear, RowParallelLinear, tp_rank_size
+from .norm import RMSNorm
+from .rotary_embedding import apply_partial_rotary
+
+
+class GatedAttention(nn.Module):
+    def __init__(self, hidden_size: int, qk_head_dim: int, num_q_heads: int, v_head_dim: int, num_kv_heads: int,
+                 attention_bias: bool, rms_norm_eps: float) -> None:
+        super().__init__()
+        self.tp_rank, self.tp_size = tp_rank_size()
+        assert num_q_heads % self.tp_size == 0
+        self.hidden_size = hidden_size
+        self.qk_head_dim, self.v_head_dim = qk_head_dim, v_head_dim
+        self.total_num_q_heads, self.total_num_kv_heads = num_q_heads, num_kv_heads
+        self.num_q_heads = num_q_heads // self.tp_size
+        self.attention_bias = attention_bias
+        self.rms_norm_eps = rms_norm_eps
+        self.scale = qk_head_dim ** -0.5
+        self.q_proj = GatedQParallelLinear(hidden_size, qk_head_dim, num_q_heads, bias=attention_bias)
+        self.k_proj = KVParallelLinear(hidden_size, qk_head_dim, num_kv_heads, bias=attention_bias)
+        self.v_proj = KVParallelLinear(hidden_size, v_head_dim, num_kv_heads, bias=attention_bias)
+        self.num_kv_heads = self.k_proj.num_kv_heads
+        self.q_norm = RMSNorm((qk_head_dim,), rms_norm_eps, True)
+        self.k_norm = RMSNorm((qk_head_dim,), rms_norm_eps, True)
+        self.o_proj = RowParallelLinear(num_q_heads * v_head_dim, hidden_size, bias=False)
+        self.k_cache: torch.Tensor = torch.empty(0)
+        self.v_cache: torch.Tensor = torch.empty(0)
+
+    @property
+    def k_nrom(self):  # the reference's attribute name (m/layers/full_attention.py:47)
+        return self.k_norm
+
+    def forward(self, x: torch.Tensor, rotary_pos_emb_cos: torch.Tensor | None,
+                rotary_pos_emb_sin: torch.Tensor | None) -> torch.Tensor:
+        ctx = get_context()
+        T = x.size(0)
+        D, Dv = self.qk_head_dim, self.v_head_dim
+        q, gate = torch.chunk(self.q_proj(x).view(T, self.num_q_heads, 2 * D), 2, dim=-1)
+        q = self.q_norm(q)
+        k = self.k_norm(self.k_proj(x).view(T, self.num_kv_heads, D))
+        v = self.v_proj(x).view(T, self.num_kv_heads, Dv)
+        if rotary_pos_emb_cos is not None and rotary_pos_emb_sin is not None:
+            q = apply_partial_rotary(q, rotary_pos_emb_cos, rotary_pos_emb_sin)
+            k = apply_partial_rotary(k, rotary_pos_emb_cos, rotary_pos_emb_sin)
+        cached = self.k_cache.numel() > 0
+        if cached and ctx.slot_mapping is not None:
+            store_kvcache(k, v, self.k_cache, self.v_cache, ctx.slot_mapping)
+        if ctx.is_prefill:
+            if cached and ctx.block_tables is not None and ctx.max_seqlen_k > ctx.max_seqlen_q:
+                o = paged_flash_attention_prefill(q, self.k_cache, self.v_cache, ctx.block_tables, ctx.context_lens,
+                                                  ctx.cu_seqlens_q, None, self.scale, ctx.block_size)
+            else:
+                o = flash_attention_prefill(q, k, v, ctx.cu_seqlens_q, self.scale, self.num_q_heads,
+                                            self.num_kv_heads, D, Dv, True)
+        else:
+            o = paged_flash_attention_decode(q, self.k_cache, self.v_cache, ctx.block_tables, ctx.context_lens,
+                                             self.scale, ctx.block_size)
+        o = o * torch.sigmoid(gate)
+        return self.o_proj(o.reshape(T, self.num_q_heads * Dv))
