@@ -29,6 +29,7 @@ import time
 
 import numpy as np
 import torch
+import torch.nn.functional as F
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -179,7 +180,7 @@ def run_c1(args, rank, world, device):
     import oracle
 
     ops = _C1Ops()
-    inp = W.c1_inputs(device, seed=rank)
+    inp = W.c1_inputs(device, seed=rank, lengths=args.lengths)
     T = inp["T"]
     clk = ClockSampler(device.index or 0).__enter__()
     time.sleep(1.0)  # let the sampler start before the work it samples
@@ -330,7 +331,7 @@ def run_c3(args, rank, world, device):
     from myvllm_b200.ops.full_attention import flash_attention_prefill
     from myvllm_b200.ops.kv_cache import store_kvcache
 
-    inp = W.c3_inputs(device, seed=rank)
+    inp = W.c3_inputs(device, seed=rank, lengths=args.lengths)
     kc = torch.zeros(inp["n_blocks"], inp["block_size"], 2, 256, dtype=torch.bfloat16, device=device)
     vc = torch.zeros_like(kc)
 
@@ -432,21 +433,41 @@ def run_c4(args, rank, world, device):
     g_ = torch.Generator(device=device).manual_seed(7)
     x0 = torch.randn(S, hidden, generator=g_, device=device, dtype=torch.bfloat16)
 
-    def step(i, x):
-        bt, cl, slots, cos, sin = meta[i]
-        set_context(False, slot_mapping=slots, context_lens=cl, block_tables=bt, block_size=bs)
+    # static buffers: the whole step is captured once as a CUDA graph and replayed with each
+    # step's metadata copied in (block tables padded to the widest step)
+    width = max(m[0].shape[1] for m in meta)
+    meta = [(F.pad(bt, (0, width - bt.shape[1])), cl, sl, c, s_) for bt, cl, sl, c, s_ in meta]
+    st_bt, st_cl, st_sl, st_cos, st_sin = (t.clone() for t in meta[0])
+    x_in = x0.clone()
+
+    def load_meta(i):
+        for dst, src in zip((st_bt, st_cl, st_sl, st_cos, st_sin), meta[i]):
+            dst.copy_(src, non_blocking=True)
+
+    def step_static():
+        set_context(False, slot_mapping=st_sl, context_lens=st_cl, block_tables=st_bt, block_size=bs)
+        res = x_in.clone()
+        h = None
         for (norm, mixer), kind in zip(layers, kinds):
-            h = norm(x)
-            if kind == "gdn":
-                h = mixer(h, None, idx, idx, False)
+            if h is None:
+                normed = norm(res)
             else:
-                h = mixer(h, cos, sin)
-            x = x + h
-        return x
+                normed, res = norm(h, residual=res)  # res += h; normed = rms(res)
+            h = mixer(normed, None, idx, idx, False) if kind == "gdn" else mixer(normed, st_cos, st_sin)
+        return res + h
 
     with torch.no_grad():
-        for i in range(args.warmup):
-            step(i, x0)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(args.warmup):
+                load_meta(i)
+                step_static()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        load_meta(args.warmup)
+        with torch.cuda.graph(graph):
+            out_static = step_static()
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
@@ -456,7 +477,8 @@ def run_c4(args, rank, world, device):
         clk.mark_start()
         s0.record()
         for i in range(args.steps):
-            step(args.warmup + i, x0)
+            load_meta(args.warmup + i)
+            graph.replay()
         s1.record()
         torch.cuda.synchronize()
         clk.mark_stop()
@@ -465,15 +487,17 @@ def run_c4(args, rank, world, device):
         # end to end: hidden states in from pinned host memory, out to pinned host memory
         xh = x0.cpu().pin_memory()
         oh = torch.empty_like(xh).pin_memory()
-        xd = torch.empty_like(x0)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for i in range(3):
-            xd.copy_(xh, non_blocking=True)
-            oh.copy_(step(args.warmup + args.steps + i % 4, xd), non_blocking=True)
+            x_in.copy_(xh, non_blocking=True)
+            load_meta(args.warmup + args.steps + i % 4)
+            graph.replay()
+            oh.copy_(out_static, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / 3
+        del graph  # graphs holding NCCL work are released before the process group
     if world > 1:
         t = torch.tensor([ms, e2e_ms], device=device, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -491,7 +515,8 @@ def run_c4(args, rank, world, device):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "c4: 36 GDN + 12 gated-attention layers, hidden 2048, 128 seqs, ctx ~U[1024,32768]",
-                       "parallelism": f"tp{world}", "l2": "KV and states far larger than L2"},
+                       "parallelism": f"tp{world}", "l2": "KV and states far larger than L2",
+                       "execution": "one CUDA graph per decode step"},
             "roofline": {"bound": "hbm", "kernel": "whole decode step (per rank)", "achieved": gbs,
                          "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": src,
                          "bytes_per_step_rank0": step_bytes, "traffic": None},
@@ -532,8 +557,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3", "c4"])
+    ap.add_argument("--lengths", default=None,
+                    help="c1/c3: sequence lengths instead of the config's seeded draw, e.g. 8x2048 or 700,1500 "
+                         "(smaller cases for profiler captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.lengths:
+        if "x" in args.lengths:
+            n, length = args.lengths.split("x")
+            args.lengths = [int(length)] * int(n)
+        else:
+            args.lengths = [int(v) for v in args.lengths.split(",")]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

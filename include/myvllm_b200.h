@@ -20,6 +20,7 @@
  *   mvb_store_kvcache           (no kernel in the reference; layout from m/ops/full_attention.py:186-195,
  *                                slot_mapping convention from m/utils/context.py:15)
  *   mvb_rmsnorm_gated           m/layers/norm.py:44-58                RMSNormGated.forward
+ *   mvb_rmsnorm                 m/layers/norm.py:6-41                 RMSNorm.forward
  *
  * Conventions kept from the reference:
  *   - index tensors (cu_seqlens, *_indices, block_tables, context_lens, slot_mapping) are int32;
@@ -151,6 +152,12 @@ int mvb_store_kvcache(const mvb_tensor* k, const mvb_tensor* v, mvb_tensor* k_ca
  * x, gate, out [N, D]; weight [D]. */
 int mvb_rmsnorm_gated(const mvb_tensor* x, const mvb_tensor* gate, const mvb_tensor* weight, float eps,
                       mvb_tensor* out, void* stream);
+
+/* s = x (+ residual, written back to residual); out = s * rsqrt(mean(s^2) + eps) * (weight
+ * [+ 1 with zero_centered_gamma]), per row.  x, residual, out [N, D] 16-bit; weight [D].
+ * Replaces RMSNorm.forward (m/layers/norm.py:6-41). */
+int mvb_rmsnorm(const mvb_tensor* x, mvb_tensor* residual, const mvb_tensor* weight, float eps,
+                int zero_centered_gamma, mvb_tensor* out, void* stream);
 
 /* Diagnostics. */
 

@@ -54,6 +54,7 @@ SIGNATURES = {
     "mvb_paged_attention_prefill": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int, _T, _P]),
     "mvb_store_kvcache": (ctypes.c_int, [_T, _T, _T, _T, _T, _P]),
     "mvb_rmsnorm_gated": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, _T, _P]),
+    "mvb_rmsnorm": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, ctypes.c_int, _T, _P]),
     "mvb_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "mvb_selftest_umma": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          ctypes.c_int, _P]),

@@ -6,8 +6,10 @@
 // Hq / Hkv query heads of that kv-head together, so each cached K/V row crosses HBM
 // once:
 //   S[g, t] = scale q_g . k_t ;  online softmax over t (exp2, fp32) ;  O[g] = sum p v_t
-// Tiles of 64 tokens are gathered through the block table with 16-byte cp.async into
-// an XOR-swizzled, double-buffered shared-memory ring; each of the 4 warps takes 16
+// Tiles of 64 tokens are gathered through the block table (the split's entries are first
+// copied to shared memory) with 16-byte cp.async into an XOR-swizzled NSTAGE-deep
+// shared-memory ring, so NSTAGE-1 tiles are in flight while one is computed; when the
+// block size is a multiple of 64 a tile lies in one page.  Each of the 4 warps takes 16
 // tokens of a tile and runs QK^T and PV on mma.sync m16n8k16 (G padded to 16 rows;
 // the padded rows are never written).  Long contexts are split across CTAs
 // (flash-decoding); split results (normalised O and log2-sum-exp) go to the caller's
@@ -38,13 +40,17 @@ namespace {
 constexpr int kTile = 64;
 constexpr int kWarps = 4;
 
+constexpr int kMaxSplitPages = 1024;  // block-table entries of one split cached in smem
+
 template <int D>
 struct DecodeSmem {
+  static constexpr int kStages = D >= 256 ? 3 : 4;
   static constexpr int kRowBytes = D * 2;
   static constexpr int kTileBytes = kTile * kRowBytes;
   static constexpr int kStageBytes = 2 * kTileBytes;  // K + V
   static constexpr int kQBytes = 16 * kRowBytes;
-  static constexpr int kBytes = 2 * kStageBytes + kQBytes;
+  static constexpr int kPagesBytes = kMaxSplitPages * 4;
+  static constexpr int kBytes = kStages * kStageBytes + kQBytes + kPagesBytes;
 };
 
 // Byte offset of 16-byte chunk `c` of row `r` in a swizzled [rows][D] bf16 tile.
@@ -53,19 +59,40 @@ __device__ __forceinline__ int swz(int r, int c) {
   return r * (D * 2) + ((c ^ (r & 7)) << 4);
 }
 
+// Block-table entry for token t: from the split's smem copy when it holds it.
+__device__ __forceinline__ int page_of(const DecodeParams& p, const int* spages, int page0, int npages, int seq,
+                                       int t) {
+  const int pg = t / p.block_size;
+  return (pg - page0 < npages) ? spages[pg - page0] : p.bt[seq * p.sbt_s + pg * p.sbt_b];
+}
+
 template <typename T, int D>
-__device__ __forceinline__ void load_tile(const DecodeParams& p, char* sK, char* sV, int seq, int kvh, int t0,
-                                          int ctx) {
+__device__ __forceinline__ void load_tile(const DecodeParams& p, char* sK, char* sV, const int* spages, int page0,
+                                          int npages, int seq, int kvh, int t0, int ctx) {
   constexpr int CH = D / 8;  // 16-byte chunks per row
   const char* kc = static_cast<const char*>(p.kc);
   const char* vc = static_cast<const char*>(p.vc);
+  if (p.block_size % kTile == 0) {  // the whole tile lies in one page
+    const int64_t blk = page_of(p, spages, page0, npages, seq, t0);
+    const int off0 = t0 % p.block_size;
+    const char* kb = kc + (blk * p.skc_b + kvh * p.skc_h) * 2;
+    const char* vb = vc + (blk * p.svc_b + kvh * p.svc_h) * 2;
+    for (int i = threadIdx.x; i < kTile * CH; i += kWarps * 32) {
+      const int r = i / CH, c = i % CH;
+      const bool ok = t0 + r < ctx;
+      const int64_t row = ok ? off0 + r : 0;
+      cp_async16(sK + swz<D>(r, c), kb + row * p.skc_t * 2 + c * 16, ok);
+      cp_async16(sV + swz<D>(r, c), vb + row * p.svc_t * 2 + c * 16, ok);
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < kTile * CH; i += kWarps * 32) {
     const int r = i / CH, c = i % CH;
     const int t = t0 + r;
     const bool ok = t < ctx;
     int64_t koff = 0, voff = 0;
     if (ok) {
-      const int blk = p.bt[seq * p.sbt_s + (t / p.block_size) * p.sbt_b];
+      const int64_t blk = page_of(p, spages, page0, npages, seq, t);
       const int off = t % p.block_size;
       koff = (blk * p.skc_b + off * p.skc_t + kvh * p.skc_h) * 2 + c * 16;
       voff = (blk * p.svc_b + off * p.svc_t + kvh * p.svc_h) * 2 + c * 16;
@@ -78,8 +105,10 @@ __device__ __forceinline__ void load_tile(const DecodeParams& p, char* sK, char*
 template <typename T, int D>
 __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams p) {
   using SM = DecodeSmem<D>;
+  constexpr int NS = SM::kStages;
   extern __shared__ __align__(128) char smem[];
-  char* sQ = smem + 2 * SM::kStageBytes;
+  char* sQ = smem + NS * SM::kStageBytes;
+  int* spages = reinterpret_cast<int*>(sQ + SM::kQBytes);
   const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ctx = p.ctx[seq];
@@ -111,9 +140,21 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams 
     }
   }
 
+  // this split's block-table entries -> smem
+  const int page0 = t_begin / p.block_size;
+  const int npages = min((t_end - 1) / p.block_size - page0 + 1, kMaxSplitPages);
+  for (int i = tid; i < npages; i += kWarps * 32) spages[i] = p.bt[seq * p.sbt_s + (page0 + i) * p.sbt_b];
+  __syncthreads();
+
   const int n_tiles = (t_end - t_begin + kTile - 1) / kTile;
-  load_tile<T, D>(p, smem, smem + SM::kTileBytes, seq, kvh, t_begin, t_end);
-  cp_async_commit();
+#pragma unroll
+  for (int st = 0; st < NS - 1; ++st) {
+    if (st < n_tiles) {
+      char* b = smem + st * SM::kStageBytes;
+      load_tile<T, D>(p, b, b + SM::kTileBytes, spages, page0, npages, seq, kvh, t_begin + st * kTile, t_end);
+    }
+    cp_async_commit();
+  }
 
   float acc[D / 8][4];
 #pragma unroll
@@ -121,14 +162,15 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams 
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows lane/4 and lane/4 + 8
 
   for (int it = 0; it < n_tiles; ++it) {
-    const int stage = it & 1;
-    if (it + 1 < n_tiles) {
-      char* nb = smem + (stage ^ 1) * SM::kStageBytes;
-      load_tile<T, D>(p, nb, nb + SM::kTileBytes, seq, kvh, t_begin + (it + 1) * kTile, t_end);
+    const int stage = it % NS;
+    cp_async_wait<NS - 2>();  // tile `it` has landed
+    __syncthreads();          // ... for every thread, and stage (it - 1) % NS is free again
+    if (it + NS - 1 < n_tiles) {
+      char* nb = smem + ((it + NS - 1) % NS) * SM::kStageBytes;
+      load_tile<T, D>(p, nb, nb + SM::kTileBytes, spages, page0, npages, seq, kvh, t_begin + (it + NS - 1) * kTile,
+                      t_end);
     }
     cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
     const char* sK = smem + stage * SM::kStageBytes;
     const char* sV = sK + SM::kTileBytes;
 
@@ -203,9 +245,9 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams 
       mma16816<T>(acc[nn * 2], pa, b);
       mma16816<T>(acc[nn * 2 + 1], pa, b + 2);
     }
-    __syncthreads();  // stage is free for the next prefetch
   }
   cp_async_wait<0>();
+  __syncthreads();  // the ring is reused for the cross-warp merge below
 
   // Row sums across the 4 lanes of a quad.
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);

@@ -14,6 +14,18 @@ from torch import nn
 from .. import _lib
 
 
+def _rows(x: torch.Tensor):
+    """x [..., d] as a 2-D [rows, d] view with one row stride (no copy), or None."""
+    if x.dim() < 2 or x.stride(-1) != 1:
+        return None
+    stride = x.stride(-2)
+    for i in range(x.dim() - 2):
+        if x.shape[i + 1] > 1 and x.stride(i) != x.stride(i + 1) * x.shape[i + 1]:
+            return None
+    rows = x.numel() // x.shape[-1]
+    return torch.as_strided(x, (rows, x.shape[-1]), (stride, 1))
+
+
 class RMSNorm(nn.Module):
     def __init__(self, normalized_shape: tuple[int, ...], eps: float = 1e-5, zero_centered_gamma=False):
         super().__init__()
@@ -25,7 +37,21 @@ class RMSNorm(nn.Module):
     def gamma(self):
         return self.weight
 
-    def rms_forward(self, x: torch.Tensor) -> torch.Tensor:
+    def rms_forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """One fused kernel on CUDA bf16/fp16 tensors (``mvb_rmsnorm``); eager fp32 math
+        otherwise (CPU tensors, fp32)."""
+        d = x.shape[-1]
+        xs = _rows(x)
+        if x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0 and d <= 2048 and \
+                xs is not None and (residual is None or residual.is_contiguous()):
+            out = torch.empty(xs.shape, dtype=x.dtype, device=x.device)
+            res = _lib.desc(residual.view(-1, d)) if residual is not None else None
+            _lib.call("RMSNorm", "mvb_rmsnorm", _lib.desc(xs), res, _lib.desc(self.weight.detach()), float(self.eps),
+                      int(self.zero_centered_gamma), _lib.desc(out), _lib.stream_of(x))
+            return out.view(x.shape)
+        if residual is not None:
+            residual.copy_(x + residual)
+            x = residual
         weight = self.weight.to(torch.float32)
         if self.zero_centered_gamma:
             weight = weight + 1.0
@@ -34,11 +60,11 @@ class RMSNorm(nn.Module):
         return y.to(x.dtype)
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None):
-        """Returns ``rms(x)`` (the reference returns ``(rms(x), x)`` without a residual,
-        ``norm.py:40``, which no caller uses; with a residual, ``(rms(x + r), x + r)``)."""
+        """``rms(x)``; with ``residual``: ``(rms(x + residual), x + residual)``, the sum also
+        written into ``residual`` (the fused pre-norm of a decoder step).  The reference
+        returns ``(rms(x), x)`` without a residual (``norm.py:40``), which no caller uses."""
         if residual is not None:
-            x = x + residual
-            return self.rms_forward(x), x
+            return self.rms_forward(x, residual), residual
         return self.rms_forward(x)
 
 

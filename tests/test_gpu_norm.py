@@ -21,3 +21,36 @@ def test_rmsnorm_gated(d):
     xf = x.float()
     ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w * torch.nn.functional.silu(z.float())
     assert_close(out, ref)
+
+
+@pytest.mark.parametrize("d", [256, 2048])
+@pytest.mark.parametrize("residual", [False, True])
+def test_rmsnorm_zero_centered_and_residual(d, residual):
+    from myvllm_b200.layers.norm import RMSNorm
+
+    g = torch.Generator().manual_seed(d + residual)
+    norm = RMSNorm((d,), 1e-6, True).cuda()
+    norm.weight.data.normal_(0, 0.1, generator=None)
+    x = torch.randn(77, d, generator=g).to(torch.bfloat16).cuda()
+    r = torch.randn(77, d, generator=g).to(torch.bfloat16).cuda()
+    r0 = r.clone()
+    if residual:
+        out, s = norm(x, residual=r)
+        base = (x.float() + r0.float())
+        assert_close(s, base)
+    else:
+        out = norm(x)
+        base = x.float()
+    ref = base * torch.rsqrt(base.pow(2).mean(-1, keepdim=True) + 1e-6) * (norm.weight.float() + 1)
+    assert_close(out, ref)
+
+
+def test_rmsnorm_strided_head_rows():
+    from myvllm_b200.layers.norm import RMSNorm
+
+    norm = RMSNorm((256,), 1e-6, True).cuda()
+    qg = torch.randn(9, 16, 512, device="cuda").to(torch.bfloat16)
+    q = qg[..., :256]  # strided head rows, as q of the gated q projection
+    out = norm(q)
+    qf = q.float()
+    assert_close(out, qf * torch.rsqrt(qf.pow(2).mean(-1, keepdim=True) + 1e-6) * 2.0)
