@@ -364,7 +364,7 @@ def run_c3(args, rank, world, device):
             "value": inp["T"] / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "c3: Hq16/Hkv2/D256 causal, 8 seqs ~U[1024,16384]", "tokens": inp["T"]},
-            "roofline": {"bound": "tensor", "kernel": "flash_prefill_kernel", "achieved": tf,
+            "roofline": {"bound": "tensor", "kernel": "fa_tc_kernel", "achieved": tf,
                          "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": tf / pk["bf16_tflops"],
                          "peak_source": src, "launch_ms": fa_ms, "flops_per_launch": flops,
                          "traffic": profiled_traffic("flash_prefill_c3")},

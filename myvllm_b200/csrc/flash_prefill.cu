@@ -1,4 +1,6 @@
-// Varlen (causal) flash attention for prefill, GQA, head dim 64/128/256.
+// Varlen (causal) flash attention for prefill, GQA, head dim 64/128/256: the mma.sync kernel
+// for layouts the tcgen05 kernel (flash_prefill_tc.cu) does not take, e.g. paged caches whose
+// block size does not tile into its K/V tiles or outputs without 16-byte rows.
 //
 // Replaces flash_attention_varlen_kernel (m/ops/full_attention.py:6-111): same math
 // (online softmax in fp32, q-head h reads kv-head h / (Hq / Hkv), optional causal mask),
@@ -11,7 +13,7 @@
 // tile are adjacent in launch order so their shared K/V tiles are L2 hits; tiles are
 // numbered per sequence on device (no host sync) and the last (most expensive under the
 // causal mask) query tiles of each sequence are issued first.
-#include "common.cuh"
+#include "flash_prefill.cuh"
 
 namespace mvb {
 namespace {
@@ -20,60 +22,9 @@ constexpr int BM = 128;
 constexpr int BN = 64;
 constexpr int kWarps = 8;
 
-struct FaParams {
-  const void *q, *k, *v;
-  void* o;
-  const int32_t* cu;
-  int64_t sq_t, sq_h, sk_t, sk_h, sv_t, sv_h, so_t, so_h;
-  // paged K/V (paged prefill): k/v are the caches [NB, bs, Hkv, D]; strides sk_b/sk_t/sk_h
-  const int32_t* bt;
-  const int32_t* ctx;
-  int64_t sk_b, sv_b, sbt_s, sbt_b;
-  int block_size;
-  int n_seqs, hq, hkv, causal;
-  float scale_log2;
-};
-
 template <int D>
 __device__ __forceinline__ int swz(int r, int c) {
   return r * (D * 2) + ((c ^ (r & 7)) << 4);
-}
-
-// tile index -> (seq, q-tile start), tiles of each sequence issued last-first
-__device__ __forceinline__ bool map_tile(const int32_t* cu, int n_seqs, int tile_idx, int& seq, int& q0) {
-  __shared__ int s_seq, s_q0;
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    int base = 0, found = -1, fq = 0;
-    for (int s0 = 0; s0 < n_seqs && found < 0; s0 += 32) {
-      const int s = s0 + lane;
-      int cnt = 0;
-      if (s < n_seqs) cnt = (cu[s + 1] - cu[s] + BM - 1) / BM;
-      int incl = cnt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const int excl = base + incl - cnt;
-      const bool hit = s < n_seqs && tile_idx >= excl && tile_idx < excl + cnt;
-      const unsigned m = __ballot_sync(0xffffffffu, hit);
-      if (m) {
-        const int src = __ffs(m) - 1;
-        found = __shfl_sync(0xffffffffu, s, src);
-        fq = __shfl_sync(0xffffffffu, (cnt - 1 - (tile_idx - excl)) * BM, src);
-      }
-      base += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) {
-      s_seq = found;
-      s_q0 = fq;
-    }
-  }
-  __syncthreads();
-  seq = s_seq;
-  q0 = s_q0;
-  return seq >= 0;
 }
 
 // PAGED: queries of sequence s sit at positions ctx[s] - L_s + i and attend to the
@@ -88,7 +39,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) flash_prefill_kernel(FaParams 
   char* sKV = smem + BM * ROWB;      // 2 stages x (K [BN][D], V [BN][D])
 
   int seq, q0;
-  if (!map_tile(p.cu, p.n_seqs, blockIdx.y, seq, q0)) return;
+  if (!map_query_tile<BM>(p.cu, p.n_seqs, blockIdx.y, seq, q0)) return;
   const int h = blockIdx.x;
   const int kvh = h / (p.hq / p.hkv);
   const int start = p.cu[seq];
@@ -328,7 +279,8 @@ extern "C" int mvb_flash_attention_prefill(const mvb_tensor* q, const mvb_tensor
   p.n_seqs = (int)n_seqs; p.hq = num_heads; p.hkv = num_kv_heads; p.causal = is_causal ? 1 : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.bt = nullptr; p.ctx = nullptr; p.sk_b = p.sv_b = p.sbt_s = p.sbt_b = 0; p.block_size = 1;
-  dispatch_fa<false>(q->dtype, head_dim, p, T, static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (launch_fa_tc(p, q->dtype, head_dim, false, T, T, 0, st) < 0) dispatch_fa<false>(q->dtype, head_dim, p, T, st);
   MVB_CHECK_LAUNCH(op);
   return MVB_OK;
 }
@@ -384,7 +336,8 @@ extern "C" int mvb_paged_attention_prefill(const mvb_tensor* q, const mvb_tensor
   p.block_size = block_size;
   p.n_seqs = (int)n_seqs; p.hq = (int)hq; p.hkv = (int)hkv; p.causal = 1;
   p.scale_log2 = scale * 1.4426950408889634f;
-  dispatch_fa<true>(q->dtype, (int)d, p, T, static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (launch_fa_tc(p, q->dtype, (int)d, true, T, 0, k_cache->shape[0], st) < 0) dispatch_fa<true>(q->dtype, (int)d, p, T, st);
   MVB_CHECK_LAUNCH(op);
   return MVB_OK;
 }

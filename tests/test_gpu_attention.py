@@ -172,3 +172,40 @@ def test_paged_prefill_with_prior_context_vs_oracle():
     ref = oracle.attention.paged_prefill(to_np(q), to_np(kc), to_np(vc), bt.clamp_min(0).numpy(), ctx, cu.numpy(),
                                          128 ** -0.5)
     assert_close(o, ref)
+
+
+@pytest.mark.parametrize("bs", [16, 48, 128, 256])
+@pytest.mark.parametrize("d", [64, 256])
+def test_paged_prefill_block_sizes_vs_oracle(bs, d):
+    """Block sizes below, inside and above the 64-key K/V tile (16: four pages per tile;
+    48: pages straddle tiles, served by the mma.sync kernel; 128/256: one page segment)."""
+    ctx = [700, 40, 129, 1]
+    new = [300, 40, 64, 1]
+    kc, vc, bt = _paged(ctx, 2, d, bs, seed=bs + d)
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(sum(new), 8, d, generator=g).to(torch.bfloat16)
+    cu = W.cu_from_lengths(new, "cpu")
+    o = paged_flash_attention_prefill(q.to(dev), kc.to(dev), vc.to(dev), bt.to(dev),
+                                      torch.tensor(ctx, dtype=torch.int32, device=dev), cu.to(dev), None,
+                                      d ** -0.5, bs)
+    ref = oracle.attention.paged_prefill(to_np(q), to_np(kc), to_np(vc), bt.clamp_min(0).numpy(), ctx, cu.numpy(),
+                                         d ** -0.5)
+    assert_close(o, ref)
+
+
+@pytest.mark.parametrize("d", [128, 256])
+def test_varlen_prefill_fp16_and_strided_q(d):
+    """fp16 operands, and q/k/v as column slices of one packed [T, (Hq + 2 Hkv) D] buffer."""
+    lens = [513, 64, 1000]
+    T, hq, hkv = sum(lens), 8, 2
+    g = torch.Generator().manual_seed(d)
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, generator=g).to(torch.float16)
+    q = qkv[:, :hq * d].view(T, hq, d)
+    k = qkv[:, hq * d:(hq + hkv) * d].view(T, hkv, d)
+    v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+    cu = W.cu_from_lengths(lens, "cpu")
+    qkv_d = qkv.to(dev)
+    o = flash_attention_prefill(qkv_d[:, :hq * d].view(T, hq, d), qkv_d[:, hq * d:(hq + hkv) * d].view(T, hkv, d),
+                                qkv_d[:, (hq + hkv) * d:].view(T, hkv, d), cu.to(dev), d ** -0.5, hq, hkv, d, d, True)
+    ref = oracle.attention.varlen(to_np(q), to_np(k), to_np(v), cu.numpy(), d ** -0.5, True)
+    assert_close(o, ref)
