@@ -19,13 +19,9 @@
 // TMEM: O in columns [0, D), score buffers at D and D + BN (512 columns allocated).
 // Every wait is bounded; a wait that gives up sets the device error word and the CTA
 // drains its copies, frees TMEM and exits.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
-
 #include "flash_prefill.cuh"
 #include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace mvb {
 namespace {
@@ -72,32 +68,6 @@ struct FaTcParams {
 constexpr int kThreads = 192;
 constexpr int kErrFa = 3;
 
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(dst),
-      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
-      "%5}], [%6];" ::"r"(dst),
-      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -155,15 +125,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && n_tiles > 0) {
-      prefetch_map(&p.tm_q);
-      prefetch_map(&p.tm_k);
-      prefetch_map(&p.tm_v);
-      mbar_expect_tx(&bars->q_full, C::Q_BYTES);
+      tma::prefetch_map(&p.tm_q);
+      tma::prefetch_map(&p.tm_k);
+      tma::prefetch_map(&p.tm_v);
+      tma::expect_tx(&bars->q_full, C::Q_BYTES);
       for (int b = 0; b < DB; ++b)
-        tma_load_3d(smem_u32(smem + b * BM * 128), &p.tm_q, b * 64, h, start + q0, &bars->q_full);
+        tma::load_3d((smem + b * BM * 128), &p.tm_q, b * 64, h, start + q0, &bars->q_full);
       // one K or V tile: DB column blocks of [BN keys][64 dims]
       auto load_tile = [&](const CUtensorMap* map, char* dst, int j0, uint64_t* bar) {
-        mbar_expect_tx(bar, C::KV_BYTES);
+        tma::expect_tx(bar, C::KV_BYTES);
         if constexpr (PAGED) {
           const int bs = p.block_size, rows = p.page_rows;
           const int last_page = (kv_len - 1) / bs;  // pages past the context hold no keys
@@ -172,11 +142,11 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
             const int page = min(key / bs, last_page);
             const int blk = p.bt[(int64_t)seq * p.sbt_s + (int64_t)page * p.sbt_b];
             for (int b = 0; b < DB; ++b)
-              tma_load_4d(smem_u32(dst + b * BN * 128 + g * 128), map, b * 64, kvh, key % bs, blk, bar);
+              tma::load_4d((dst + b * BN * 128 + g * 128), map, b * 64, kvh, key % bs, blk, bar);
           }
         } else {
           for (int b = 0; b < DB; ++b)
-            tma_load_3d(smem_u32(dst + b * BN * 128), map, b * 64, kvh, start + j0, bar);
+            tma::load_3d((dst + b * BN * 128), map, b * 64, kvh, start + j0, bar);
         }
       };
       int k_issued = 0, v_issued = 0;
@@ -256,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       tmem_wait_ld();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->s_free[j & 1]);
+      if (lane == 0) tma::arrive(&bars->s_free[j & 1]);
 
       const int j0 = j * BN;
       const bool need_mask = (j0 + BN > kv_len) || (p.causal && j0 + BN - 1 > qoff + q0);
@@ -306,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       fence_async_smem();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[j & 1]);
+      if (lane == 0) tma::arrive(&bars->p_full[j & 1]);
     }
     if (ok && n_tiles > 0) ok = warp_wait(&bars->o_done, 0);
     if (ok) {
@@ -344,34 +314,6 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
 }
 
 // ------------------------------------------------------------------ host side ----
-// The driver's tensor-map encoder, looked up through the runtime so that the library has no
-// link-time dependency on libcuda (it loads on hosts without a driver).
-PFN_cuTensorMapEncodeTiled_v12000 encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-bool encode(CUtensorMap* map, int dtype, int rank, const void* base, const cuuint64_t* dims,
-            const cuuint64_t* strides_bytes, const cuuint32_t* box) {
-  const auto fn = encoder();
-  if (fn == nullptr) return false;
-  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  const CUtensorMapDataType dt =
-      dtype == MVB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return fn(map, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
-                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <typename T, int D, bool PAGED>
 int launch_typed(const FaParams& fp, int64_t T_q, int64_t n_tokens_kv, int64_t n_blocks, cudaStream_t st) {
   using C = FaTc<D>;
@@ -382,7 +324,7 @@ int launch_typed(const FaParams& fp, int64_t T_q, int64_t n_tokens_kv, int64_t n
     const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)fp.hq, (cuuint64_t)T_q};
     const cuuint64_t str[2] = {(cuuint64_t)fp.sq_h * 2, (cuuint64_t)fp.sq_t * 2};
     const cuuint32_t box[3] = {64, 1, (cuuint32_t)C::BM};
-    if (!encode(&p.tm_q, dtype, 3, fp.q, dims, str, box)) return -1;
+    if (!tma::encode(&p.tm_q, dtype, 3, fp.q, dims, str, box)) return -1;
   }
   if constexpr (PAGED) {
     const int rows = fp.block_size < C::BN ? fp.block_size : C::BN;
@@ -390,14 +332,14 @@ int launch_typed(const FaParams& fp, int64_t T_q, int64_t n_tokens_kv, int64_t n
     const cuuint64_t sk[3] = {(cuuint64_t)fp.sk_h * 2, (cuuint64_t)fp.sk_t * 2, (cuuint64_t)fp.sk_b * 2};
     const cuuint64_t sv[3] = {(cuuint64_t)fp.sv_h * 2, (cuuint64_t)fp.sv_t * 2, (cuuint64_t)fp.sv_b * 2};
     const cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
-    if (!encode(&p.tm_k, dtype, 4, fp.k, dims, sk, box) || !encode(&p.tm_v, dtype, 4, fp.v, dims, sv, box)) return -1;
+    if (!tma::encode(&p.tm_k, dtype, 4, fp.k, dims, sk, box) || !tma::encode(&p.tm_v, dtype, 4, fp.v, dims, sv, box)) return -1;
     p.page_rows = rows;
   } else {
     const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)fp.hkv, (cuuint64_t)n_tokens_kv};
     const cuuint64_t sk[2] = {(cuuint64_t)fp.sk_h * 2, (cuuint64_t)fp.sk_t * 2};
     const cuuint64_t sv[2] = {(cuuint64_t)fp.sv_h * 2, (cuuint64_t)fp.sv_t * 2};
     const cuuint32_t box[3] = {64, 1, (cuuint32_t)C::BN};
-    if (!encode(&p.tm_k, dtype, 3, fp.k, dims, sk, box) || !encode(&p.tm_v, dtype, 3, fp.v, dims, sv, box)) return -1;
+    if (!tma::encode(&p.tm_k, dtype, 3, fp.k, dims, sk, box) || !tma::encode(&p.tm_v, dtype, 3, fp.v, dims, sv, box)) return -1;
     p.page_rows = C::BN;
   }
   p.o = fp.o;

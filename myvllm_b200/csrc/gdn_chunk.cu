@@ -4,11 +4,12 @@
 // tensor-core kernel of gdn_chunk_tc.cu; fp32 inputs and other head sizes run the
 // token-serial recurrence of gdn_recurrent.cu (exact fp32 math, same results).
 //
-// Precision of the tensor-core path: all contractions take fp16 operands with fp32
-// accumulation.  bf16 q/k/v convert to fp16 exactly (for 6e-5 < |x| < 65504; smaller
-// magnitudes keep their absolute accuracy); the internal operands (Ti, w, the fp16 copy of
-// the state, v_new) are rounded to fp16 (2^-11 relative) instead of bf16 (2^-8), which keeps
-// the final fp32 state within 1e-3 relative (measured ~2e-4) of the exact recurrence.
+// Precision of the tensor-core path: the input-side contractions ([q;k]k^T and the U/W
+// products) take the bf16/fp16 inputs as they are, with the 64x64 triangular factors split
+// into 16-bit hi + lo parts; the state-side contractions take fp16 operands (the fp16 copy
+// of the state, q', k', W, v_new, Aqk: 2^-11 relative instead of bf16's 2^-8); every
+// accumulator is fp32.  This keeps the final fp32 state within 1e-3 relative (measured
+// ~2e-4) of the exact recurrence.
 #include "common.cuh"
 
 namespace mvb {
@@ -37,7 +38,8 @@ int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
   if (n_seqs == 0 || v->shape[1] == 0) return MVB_OK;
   MVB_CHECK_ARG(ws == nullptr || (ws_bytes >= 8 && (reinterpret_cast<uintptr_t>(ws) & 3) == 0),
                 "%s: workspace must be at least 8 bytes, 4-byte aligned", op);
-  return launch_chunk_tc(q, k, v, g, beta, state, idx, cu, o, scale, l2norm, n_seqs, static_cast<int*>(ws), st);
+  rc = launch_chunk_tc(q, k, v, g, beta, state, idx, cu, o, scale, l2norm, n_seqs, static_cast<int*>(ws), st);
+  return rc < 0 ? run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, st) : rc;
 }
 
 }  // namespace mvb

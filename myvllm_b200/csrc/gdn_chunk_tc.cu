@@ -1,92 +1,97 @@
 // Chunked gated delta rule (prefill) on the sm_100a tensor cores: tcgen05.mma with TMEM
-// accumulators, WY form, chunk C = 64, K = V = 128.
+// accumulators, TMA-fed inputs, WY form, chunk C = 64, K = V = 128.
 //
 // Replaces the reference's six-launch pipeline (m/ops/gated_delta_rule/gated_delta_rule.py:44-64:
 // cumsum.py -> chunk_scaled_dot_kkt.py -> solve_tril.py -> wu.py -> h.py -> o.py) with one
-// persistent kernel.  A CTA walks one (sequence, v-head) chain chunk by chunk; the fp32 state
+// persistent kernel.  A CTA walks (sequence, v-head) chains chunk by chunk; the fp32 state
 // S [K, V] lives in tensor memory for the whole chain, every intermediate stays on chip, and
 // HBM sees q, k, v, g, beta once, o once and the state once per chain.
 //
-// Every contraction is written with the 128-wide feature dimension as the MMA M (the only
-// M=128 cta_group::1 shape), i.e. transposed where needed (^T on a per-chunk 64-token axis):
-//   D1   = [q; k] k^T                 (M = 64 q rows + 64 k rows, N = 64, K = 128)
-//          -> Aqk = lower(D1[q] * e^{G_i-G_j}),  A = strict_lower(beta_i D1[k] e^{G_i-G_j})
-//   Ti   = (I + A)^-1                 (blocked: 16x16 diagonal blocks by fp32 forward
-//                                      substitution, off-diagonal blocks by mma.sync with
-//                                      fp16 hi/lo operand splitting, ~fp32 accurate)
-//   U^T  = v^T (Ti diag(beta))^T      W^T = k^T (Ti diag(beta e^G))^T          (N = 64, K = 64)
-//   Vn^T = U^T - S^T W^T              (negated-A accumulate into U^T; K = 128)
-//   O1^T = S^T q^T,   O2^T = Vn^T Aqk^T,   o = scale (e^{G_i} O1 + O2)
-//   S    = e^{G_last} S + k'^T Vn     (k' = e^{G_last - G} k; N = 128, K = 64)
-// Operands are fp16 in shared memory (bf16 inputs convert exactly; see the precision note
-// in run_chunk), staged in the 128-byte-swizzle layouts of tcgen05.cuh; accumulators fp32.
+// Per chunk (^T on a per-chunk 64-token axis; every contraction has the 128-wide feature
+// dimension as the MMA M):
+//   D1   = [q; k] k^T on the raw inputs          (M = 64 q rows + 64 k rows, N = 64, K = 128)
+//          with the q/k L2 norms applied to the fp32 products:
+//          Aqk = lower(scale D1[q] e^{G_i-G_j} / |q_i||k_j|),
+//          A   = strict_lower(beta_i D1[k] e^{G_i-G_j} / |k_i||k_j|)
+//   Ti   = (I + A)^-1                           (blocked, fp32-accurate: see solve_tril64)
+//   U^T  = v^T (Ti diag(beta))^T,  W^T = k^T (Ti diag(beta e^G / |k|))^T on the raw inputs,
+//          the two 64x64 factors split into 16-bit hi + lo parts (two MMAs each)
+//   Vn^T = U^T - S^T W^T                         (negated-A accumulate into U^T; K = 128)
+//   O^T  = S^T q'^T + Vn^T Aqk^T                 (q' = scale e^{G_i} q / |q|)
+//   S    = e^{G_last} S + k'^T Vn                (k' = e^{G_last-G} k / |k|; N = 128, K = 64)
+// The state-side operands (fp16 copy of S, q', k', W, Vn, Aqk) are fp16 in shared memory,
+// accumulators fp32 (the final fp32 state stays within 1e-3 relative of the exact recurrence).
 //
-// Per chunk the CTA (256 threads = 2 warpgroups; thread t of a warpgroup owns TMEM lane t,
-// the two warpgroups split columns) runs: convert tiles (+ q/k L2 norm) and prefetch the next
-// chunk with cp.async -> MMA D1, O1 -> masks/decay -> solve -> MMA U, W -> stage W ->
-// MMA Vn -> stage Vn, scale S -> MMA O2, S-update -> epilogue (o, fp16 copy of S).
-// Chains are handed out longest sequence first over a persistent grid (one CTA per SM):
-// dynamically through a work counter when the caller supplies one (CTAs that finish early
-// take the next chain; the last CTA to run dry zeroes the counter for the next launch),
-// else round-robin.
+// Two warp groups pipeline consecutive chunks:
+//   prep (warps 0-7): TMA loads, gates, D1, masks, triangular solve, U/W, q'/k', W staging
+//                     for chunk c+1 -- nothing here depends on the state;
+//   rec  (warps 8-11, thread = TMEM lane): Vn, O and the state update for chunk c, the
+//                     output tile and the fp16 state copy for chunk c+1.
+// They hand buffers over through mbarriers (ready / gates-ready from prep; MMA completions
+// and U-buffer releases from rec).  Chains are handed out longest sequence first over a
+// persistent grid: dynamically through a work counter when the caller supplies one (the
+// last CTA to run dry zeroes it for the next launch), else round-robin.  Every wait is
+// bounded; a wait that gives up sets the device error word and the CTA winds down.
 #include <type_traits>
 
 #include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace mvb {
-
-int check_gdn(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
-              const mvb_tensor* beta, const mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
-              const mvb_tensor* o, int64_t* n_seqs_out);
-int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
-                  const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx,
-                  const mvb_tensor* cu, mvb_tensor* o, float scale, int l2norm, cudaStream_t st);
-
 namespace {
 
 constexpr int C = 64;
 constexpr int D = 128;  // K = V = 128
-constexpr int kThreads = 256;
+constexpr int kPrep = 256, kRec = 128, kThreads = kPrep + kRec;
+constexpr int kBarPrep = 1, kBarRec = 2;  // named barriers
 constexpr int kMaxSort = 512;
 
 // TMEM columns
-constexpr uint32_t COL_S = 0, COL_D1 = 128, COL_U = 192, COL_W = 256, COL_O1 = 320, COL_O2 = 384;
+constexpr uint32_t COL_S = 0, COL_O = 128, COL_U = 192 /* two 64-column buffers */, COL_W = 320, COL_D1 = 384;
 constexpr uint32_t TMEM_COLS = 512;
 
 // shared memory (bytes from the 1024-aligned base)
-constexpr uint32_t SM_QK = 0;          // [q;k] fp16, 2 K-halves x [128][128 B]
-constexpr uint32_t SM_V = 32768;       // v fp16, 2 halves x [64][128 B]
-constexpr uint32_t SM_KP = 49152;      // k' fp16
-constexpr uint32_t SM_S = 65536;       // S fp16, 2 v-halves x [128][128 B]
-constexpr uint32_t SM_W = 98304;       // w fp16 [64 tokens][128 kdim]
-constexpr uint32_t SM_VN = 114688;     // v_new fp16 [64 tokens][128 v]
-constexpr uint32_t SM_TU = 131072;     // Tu fp16 [64][64]
-constexpr uint32_t SM_TW = 139264;     // Tw fp16 [64][64]
-constexpr uint32_t SM_AQK = 147456;    // Aqk fp16 [64][64]
-constexpr uint32_t SM_A = 155648;      // A fp32 [64][64], column index XOR-swizzled by row
-constexpr uint32_t SM_T = SM_W;        // Ti fp32 [64][64] (same swizzle), aliases w (dead then)
-constexpr uint32_t SM_X = SM_VN;       // per-warp 16x16 fp32 scratch of the solve, aliases v_new
-constexpr uint32_t SM_STG = 172032;    // staging (raw inputs): q, k, v, each 2 halves x [64][128 B]
-constexpr uint32_t SM_G = 221184;      // G2 [64] f32
-constexpr uint32_t SM_B = SM_G + 256;  // beta [64] f32
-constexpr uint32_t SM_BW = SM_B + 256; // beta e^G [64] f32
-constexpr uint32_t SM_AL = SM_BW + 256; // e^{g_t} [64] f32 (per-token decay)
-constexpr uint32_t SM_EG = SM_AL + 256; // e^{G_t} [64] f32
-constexpr uint32_t SM_O = SM_W;         // o tile [64][128] of the epilogue (w is dead by then)
-constexpr uint32_t SM_PERM = SM_EG + 256;
+constexpr uint32_t SM_QK = 0;           // raw [q; k], 2 buffers x 2 K-halves x [128 rows][128 B]
+constexpr uint32_t SM_V = 65536;        // raw v, 2 halves x [64][128 B]
+constexpr uint32_t SM_QP = 81920;       // q' fp16 [64 tok][128 kdim] (2 x [64][128 B])
+constexpr uint32_t SM_KP = 98304;       // k' fp16 [64 tok][128 kdim]
+constexpr uint32_t SM_AQK = 114688;     // Aqk fp16 [64][64]
+constexpr uint32_t SM_WS = 122880;      // W^T fp16 [128 kdim][64 tok]
+constexpr uint32_t SM_TF = 139264;      // Tu hi, Tu lo, Tw hi, Tw lo: 4 x [64][64] 16-bit
+constexpr uint32_t SM_A = SM_TF;        //   before that: A fp32 [64][64] (fidx4 layout) and
+constexpr uint32_t SM_T = SM_TF + 16384;  //   Ti fp32 [64][64] (fidx layout)
+constexpr uint32_t SM_VN = 172032;      // Vn^T fp16 [128 v][64 tok]; then the o tile [64 tok][128 v]
+constexpr uint32_t SM_O = SM_VN;
+constexpr uint32_t SM_S16 = 188416;     // S fp16 [128 kdim][128 v] (2 x [128][128 B])
+constexpr uint32_t SM_X = 221184;       // solve scratch, 6 warps x 512 B
+constexpr uint32_t SM_F = 224256;       // small fp32 vectors
+// G (log2 units), beta, beta e^G, 1/|q|, 1/|k|, G - log2(1/|k|) per column, raw gates
+constexpr int F_G = 0, F_B = 64, F_BW = 128, F_QN = 192, F_KN = 256, F_GC = 320, F_GRAW = 384, F_BRAW = 448;
+constexpr uint32_t SM_PERM = SM_F + 512 * 4;
 constexpr uint32_t SMEM_BYTES = SM_PERM + kMaxSort * 4 + 1024;  // + alignment slack
+static_assert(SMEM_BYTES <= 232448 - 512, "shared memory budget");
 
 struct Params {
-  const void *q, *k, *v, *g, *beta;
+  CUtensorMap tm_q, tm_k, tm_v;
+  const void *g, *beta;
   void* o;
   float* state;
   const int32_t* state_idx;
   const int32_t* cu;
-  int64_t sq_t, sq_h, sk_t, sk_h, sv_t, sv_h, so_t, so_h, sg_t, sg_h, sb_t, sb_h;
-  int64_t ss_n, ss_h, ss_k;
+  int64_t so_t, so_h, sg_t, sg_h, sb_t, sb_h, ss_n, ss_h, ss_k;
   int* work;  // [next chain, CTAs done] or null
   int n_seqs, hk, hv, l2norm, g32, b32;
   float scale;
+};
+
+struct Bars {
+  uint64_t raw_qk[2], raw_v, d1_done, mma2_done, mma_r, ready, gready[2], r3done, r4done;
+  uint64_t d1_go, mma2_go, normed, conv_done, mma_all;
+};
+
+// chunk record handed from prep to rec
+struct Rec {
+  int seq, h, c0, n, flags;  // flags: 1 valid, 2 first chunk of its chain, 4 last chunk
 };
 
 __device__ __forceinline__ float ldg_f(const void* p, int64_t i, bool f32, bool is_bf16) {
@@ -95,8 +100,34 @@ __device__ __forceinline__ float ldg_f(const void* p, int64_t i, bool f32, bool 
   return __half2float(static_cast<const __half*>(p)[i]);
 }
 
-// fp32 [64][64] matrices of the solve: element (i, j) at i * 64 + (j ^ (i & 31)).
+__device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// Barrier over a warp group that also ANDs a flag across it (uniform abort decisions).
+__device__ __forceinline__ bool bar_and(int id, int n, bool v) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.s32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.s32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((int)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+// fp32 [64][64] matrices of the solve.  Ti: element (i, j) at i * 64 + (j ^ (i & 31)); A: groups
+// of 4 columns swizzled by row (i * 64 + 4 ((j / 4) ^ (i % 16)) + j % 4) so that rows are
+// written with 16-byte stores.
 __device__ __forceinline__ int fidx(int i, int j) { return i * 64 + (j ^ (i & 31)); }
+__device__ __forceinline__ int fidx4(int i, int j) { return i * 64 + ((((j >> 2) ^ (i & 15))) << 2) + (j & 3); }
+template <bool kA>
+__device__ __forceinline__ int midx(int i, int j) { return kA ? fidx4(i, j) : fidx(i, j); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // fp32 -> fp16 hi + lo (x ~ hi + lo to ~2^-22 relative), packed in pairs.
 __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
@@ -106,12 +137,13 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_
 }
 
 // A fragment (16x16) of block (bi, bj) of a swizzled fp32 [64][64] matrix, split hi/lo.
+template <bool kA>
 __device__ __forceinline__ void frag_a_split(uint32_t* ah, uint32_t* al, const float* M, int bi, int bj, int lane) {
   const int r = bi * 16 + (lane >> 2), c = bj * 16 + (lane & 3) * 2;
-  split2(M[fidx(r, c)], M[fidx(r, c + 1)], ah[0], al[0]);
-  split2(M[fidx(r + 8, c)], M[fidx(r + 8, c + 1)], ah[1], al[1]);
-  split2(M[fidx(r, c + 8)], M[fidx(r, c + 9)], ah[2], al[2]);
-  split2(M[fidx(r + 8, c + 8)], M[fidx(r + 8, c + 9)], ah[3], al[3]);
+  split2(M[midx<kA>(r, c)], M[midx<kA>(r, c + 1)], ah[0], al[0]);
+  split2(M[midx<kA>(r + 8, c)], M[midx<kA>(r + 8, c + 1)], ah[1], al[1]);
+  split2(M[midx<kA>(r, c + 8)], M[midx<kA>(r, c + 9)], ah[2], al[2]);
+  split2(M[midx<kA>(r + 8, c + 8)], M[midx<kA>(r + 8, c + 9)], ah[3], al[3]);
 }
 
 // acc (16x8) += A B with fp16 hi/lo operands: hi*hi + hi*lo + lo*hi (~fp32 accurate).
@@ -122,9 +154,10 @@ __device__ __forceinline__ void mma3(float* acc, const uint32_t* ah, const uint3
   mma16816<__half>(acc, al, bh);
 }
 
-// Ti = (I + A)^-1 for the strictly lower 64x64 A in sA; result (lower part) in sT.
-// Diagonal 16x16 blocks by right-looking forward substitution (threads 0-63), then for each
-// block diagonal L = 1, 2, 3 every (block (i, j = i - L), 8-column tile) pair is one warp:
+// Ti = (I + A)^-1 for the strictly lower 64x64 A in sA; result (lower part) in sT.  Run by
+// the 256 prep threads.  Diagonal 16x16 blocks by right-looking forward substitution
+// (threads 0-63), then for each block diagonal L = 1, 2, 3 every (block (i, j = i - L),
+// 8-column tile) pair is one warp:
 //   X = sum_{k=j}^{i-1} A_ik T_kj[:, tile],   T_ij[:, tile] = -T_ii X
 // with the products on mma.sync (fp16 hi/lo splitting, fp32 accumulate).
 __device__ __forceinline__ void solve_tril64(const float* sA, float* sT, float* sX, int tid) {
@@ -139,12 +172,12 @@ __device__ __forceinline__ void solve_tril64(const float* sA, float* sT, float* 
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
 #pragma unroll
-      for (int r2 = r + 1; r2 < 16; ++r2) x[r2] -= sA[fidx(base + r2, base + r)] * x[r];
+      for (int r2 = r + 1; r2 < 16; ++r2) x[r2] -= sA[fidx4(base + r2, base + r)] * x[r];
     }
 #pragma unroll
     for (int r = 0; r < 16; ++r) sT[fidx(base + r, base + c)] = x[r];
   }
-  __syncthreads();
+  bar_sync(kBarPrep, kPrep);
   const int r = lane >> 2, c2 = (lane & 3) * 2;
 #pragma unroll 1
   for (int lvl = 1; lvl < 4; ++lvl) {
@@ -153,7 +186,7 @@ __device__ __forceinline__ void solve_tril64(const float* sA, float* sT, float* 
       float X[4] = {0.f, 0.f, 0.f, 0.f};
       for (int kb = bj; kb < bi; ++kb) {
         uint32_t ah[4], al[4], bh[2], bl[2];
-        frag_a_split(ah, al, sA, bi, kb, lane);
+        frag_a_split<true>(ah, al, sA, bi, kb, lane);
         const int k = kb * 16 + c2, n = bj * 16 + nt * 8 + r;
         split2(sT[fidx(k, n)], sT[fidx(k + 1, n)], bh[0], bl[0]);
         split2(sT[fidx(k + 8, n)], sT[fidx(k + 9, n)], bh[1], bl[1]);
@@ -165,7 +198,7 @@ __device__ __forceinline__ void solve_tril64(const float* sA, float* sT, float* 
       xs[(r + 8) * 8 + c2] = X[2]; xs[(r + 8) * 8 + c2 + 1] = X[3];
       __syncwarp();
       uint32_t ah[4], al[4], bh[2], bl[2];
-      frag_a_split(ah, al, sT, bi, bi, lane);
+      frag_a_split<false>(ah, al, sT, bi, bi, lane);
       split2(xs[c2 * 8 + r], xs[(c2 + 1) * 8 + r], bh[0], bl[0]);
       split2(xs[(c2 + 8) * 8 + r], xs[(c2 + 9) * 8 + r], bh[1], bl[1]);
       float Y[4] = {0.f, 0.f, 0.f, 0.f};
@@ -174,45 +207,36 @@ __device__ __forceinline__ void solve_tril64(const float* sA, float* sT, float* 
       sT[fidx(rr, cc)] = -Y[0]; sT[fidx(rr, cc + 1)] = -Y[1];
       sT[fidx(rr + 8, cc)] = -Y[2]; sT[fidx(rr + 8, cc + 1)] = -Y[3];
     }
-    __syncthreads();
+    bar_sync(kBarPrep, kPrep);
   }
 }
 
-// One work item = (chain, chunk).  Chain j of this CTA is blockIdx.x + j * gridDim.x in the
-// longest-first order.
 struct Item {
   int seq, h, c0, n, t_end;
-  bool valid;
+  bool valid, first;
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(Params p) {
+__global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) char smem_raw[];
   char* sm = umma::align1024(smem_raw);
-  __shared__ uint64_t mbar;
+  __shared__ Bars bars;
+  __shared__ Rec recs[2];
+  __shared__ float s_el[2];  // e^{G_last} of the chunk in each record slot
   __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-  __shared__ float s_graw[C], s_braw[C];
   __shared__ int s_chain;
+  __shared__ int s_end;  // set by prep when the work runs out
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int wg = warp >> 2;          // warpgroup: splits TMEM columns
-  const int tl = tid & 127;          // TMEM lane owned by this thread
-  const int lane_base = (warp & 3) * 32;
-  float* sG = reinterpret_cast<float*>(sm + SM_G);
-  float* sB = reinterpret_cast<float*>(sm + SM_B);
-  float* sBW = reinterpret_cast<float*>(sm + SM_BW);
-  float* sAL = reinterpret_cast<float*>(sm + SM_AL);
-  float* sEG = reinterpret_cast<float*>(sm + SM_EG);
-  float* sT = reinterpret_cast<float*>(sm + SM_T);
-  float* sX = reinterpret_cast<float*>(sm + SM_X);
+  const int lane_base = (warp & 3) * 32;  // TMEM lanes this warp may access
+  const int tl = tid & 127;               // TMEM lane owned by this thread
+  float* sF = reinterpret_cast<float*>(sm + SM_F);
   int* sPerm = reinterpret_cast<int*>(sm + SM_PERM);
-  float* sA = reinterpret_cast<float*>(sm + SM_A);
   const uint32_t sbase = smem_u32(sm);
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr float LOG2E = 1.4426950408889634f;
 
-  // ---- setup: chain order, barrier, TMEM ----
+  // ---- setup: chain order, barriers, TMEM ----
   const int S = p.n_seqs;
   const bool sorted = S <= kMaxSort;
   if (sorted) {
@@ -227,434 +251,614 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(Params p) {
     }
   }
   if (tid == 0) {
-    umma::mbar_init(&mbar, 1);
+    for (int b = 0; b < 2; ++b) {
+      umma::mbar_init(&bars.raw_qk[b], 1);
+      umma::mbar_init(&bars.gready[b], 1);
+    }
+    for (uint64_t* m : {&bars.d1_go, &bars.mma2_go, &bars.normed, &bars.conv_done, &bars.mma_all})
+      umma::mbar_init(m, 1);
+    s_end = 0;
+    umma::mbar_init(&bars.raw_v, 1);
+    umma::mbar_init(&bars.d1_done, 1);
+    umma::mbar_init(&bars.mma2_done, 1);
+    umma::mbar_init(&bars.mma_r, 1);
+    umma::mbar_init(&bars.ready, 1);
+    umma::mbar_init(&bars.r3done, 1);
+    umma::mbar_init(&bars.r4done, 1);
     umma::mbar_fence_init();
-    abort_flag = 0;
   }
   if (warp == 0) umma::tmem_alloc(&tmem_slot, TMEM_COLS);
   umma::fence_before();
   __syncthreads();
   umma::fence_after();
   const uint32_t tmem = tmem_slot;
-  uint32_t phase = 0;
-
-  const T* gq = static_cast<const T*>(p.q);
-  const T* gk = static_cast<const T*>(p.k);
-  const T* gv = static_cast<const T*>(p.v);
-  T* go = static_cast<T*>(p.o);
   const int n_chains = S * p.hv;
 
-  auto chain_item = [&](int chain) -> Item {
-    Item it;
-    it.valid = chain < n_chains;
-    if (!it.valid) return it;
-    it.seq = sorted ? sPerm[chain / p.hv] : chain / p.hv;
-    it.h = chain % p.hv;
-    it.c0 = p.cu[it.seq];
-    it.t_end = p.cu[it.seq + 1];
-    it.n = min(C, it.t_end - it.c0);
-    return it;
-  };
-  // Thread 0 only: the next non-empty chain for this CTA (>= n_chains when none is left).
-  int rr = 0;
-  bool exhausted = false;
-  auto fetch = [&]() -> int {
-    for (;;) {
-      const int c = p.work ? atomicAdd(p.work, 1) : (int)blockIdx.x + (rr++) * (int)gridDim.x;
-      if (c >= n_chains) {
-        exhausted = true;
-        if (p.work && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
-          p.work[0] = 0;
-          p.work[1] = 0;
-        }
-        return c;
-      }
-      if (chain_item(c).n > 0) return c;
-    }
-  };
-  // Prefetch raw q/k/v of an item into staging (cp.async, zero rows >= n); g/beta into regs.
-  float g_pre = 0.f, b_pre = 0.f;
-  auto prefetch = [&](const Item& it) {
-    if (!it.valid) return;
-    const int kh = it.h / (p.hv / p.hk);
-    for (int i = tid; i < C * 16; i += kThreads) {
-      const int r = i >> 4, c = i & 15;
-      const bool ok = r < it.n;
-      const int t = ok ? it.c0 + r : it.c0;
-      const uint32_t off = (c >> 3) * 8192 + umma::sw128(r, c & 7);
-      cp_async16(sm + SM_STG + off, gq + t * p.sq_t + kh * p.sq_h + c * 8, ok);
-      cp_async16(sm + SM_STG + 16384 + off, gk + t * p.sk_t + kh * p.sk_h + c * 8, ok);
-      cp_async16(sm + SM_STG + 32768 + off, gv + t * p.sv_t + it.h * p.sv_h + c * 8, ok);
-    }
-    cp_async_commit();
-    if (tid < C) {
-      g_pre = tid < it.n ? ldg_f(p.g, (int64_t)(it.c0 + tid) * p.sg_t + it.h * p.sg_h, p.g32, kBf16) : 0.f;
-    } else if (tid < 2 * C) {
-      const int r = tid - C;
-      b_pre = r < it.n ? ldg_f(p.beta, (int64_t)(it.c0 + r) * p.sb_t + it.h * p.sb_h, p.b32, kBf16) : 0.f;
-    }
-  };
-  // wait for the MMAs committed so far; all threads take part
-  auto mma_wait = [&]() -> bool {
-    if (!umma::mbar_wait(&mbar, phase)) {
-      abort_flag = 1;
-      report_device_error(1);
-    }
-    phase ^= 1;
-    umma::fence_after();
-    return true;
-  };
-
-  if (tid == 0) s_chain = fetch();
-  __syncthreads();
-  int chain = s_chain;
-  Item cur = chain_item(chain);
-  prefetch(cur);
-  bool chain_start = true;
-
-  float* gstate = nullptr;
-  while (cur.valid) {
-    const int h = cur.h, c0 = cur.c0, n = cur.n;
-    const bool last_chunk = c0 + C >= cur.t_end;
-    if (chain_start) gstate = p.state + (int64_t)p.state_idx[cur.seq] * p.ss_n + (int64_t)h * p.ss_h;
-
-    // ---- chain start: state -> TMEM (fp32) and SM_S (fp16) ----
-    if (chain_start) {
-      const float* srow = gstate + (int64_t)tl * p.ss_k + wg * 64;
-#pragma unroll
-      for (int cc = 0; cc < 64; cc += 16) {
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          const float4 x = *reinterpret_cast<const float4*>(srow + cc + j);
-          v[j] = x.x; v[j + 1] = x.y; v[j + 2] = x.z; v[j + 3] = x.w;
-        }
-        umma::tmem_st16(umma::taddr(tmem, lane_base, COL_S + wg * 64 + cc), v);
-        // fp16 copy: row tl (kdim), columns wg*64 + cc .. +16 -> two 16-byte chunks
-#pragma unroll
-        for (int j = 0; j < 16; j += 8) {
-          const int col = wg * 64 + cc + j;
-          *reinterpret_cast<uint4*>(sm + SM_S + (col >> 6) * 16384 + umma::sw128(tl, (col >> 3) & 7)) =
-              pack8<__half>(v + j);
-        }
-      }
-      umma::tmem_wait_st();
-    }
-
-    // ---- A: chunk landed; G, beta ----
-    cp_async_wait<0>();
-    if (tid < C) s_graw[tid] = g_pre;
-    else if (tid < 2 * C) s_braw[tid - C] = b_pre;
-    if (last_chunk && tid == 0) s_chain = fetch();
-    __syncthreads();
-    if (warp == 0) {
-      const float g0 = s_graw[2 * lane], g1 = s_graw[2 * lane + 1];
-      float incl = g0 + g1;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      sG[2 * lane] = (incl - g1) * LOG2E;
-      sG[2 * lane + 1] = incl * LOG2E;
-      sB[2 * lane] = s_braw[2 * lane];
-      sB[2 * lane + 1] = s_braw[2 * lane + 1];
-      const float eg0 = exp2f((incl - g1) * LOG2E), eg1 = exp2f(incl * LOG2E);
-      sEG[2 * lane] = eg0;
-      sEG[2 * lane + 1] = eg1;
-      sBW[2 * lane] = s_braw[2 * lane] * eg0;
-      sBW[2 * lane + 1] = s_braw[2 * lane + 1] * eg1;
-      sAL[2 * lane] = exp2f(g0 * LOG2E);
-      sAL[2 * lane + 1] = exp2f(g1 * LOG2E);
-    }
-    __syncthreads();
-
-    // ---- B: convert staging -> fp16 operands (q, k L2-normalised; k' = e^{G_last-G} k) ----
-    {
-      const int r = tid >> 2, qq = tid & 3;  // row, quarter of the 128 columns
-      const float gl = sG[C - 1];
-      const float kscale = exp2f(gl - sG[r]);
-#pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        float f[4][8];
-        float ss = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = qq * 4 + i;
-          const uint32_t off = (c >> 3) * 8192 + umma::sw128(r, c & 7);
-          unpack8<T>(*reinterpret_cast<const uint4*>(sm + SM_STG + m * 16384 + off), f[i]);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) ss += f[i][j] * f[i][j];
-        }
-        float sc = 1.f;
-        if (p.l2norm) {
-          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-          sc = rsqrtf(ss + 1e-6f);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = qq * 4 + i;
-          float y[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) y[j] = f[i][j] * sc;
-          // [q;k]: q rows 0-63, k rows 64-127 of each 16 KB K-half
-          *reinterpret_cast<uint4*>(sm + SM_QK + (c >> 3) * 16384 + umma::sw128(r + m * 64, c & 7)) =
-              pack8<__half>(y);
-          if (m == 1) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) y[j] *= kscale;
-            *reinterpret_cast<uint4*>(sm + SM_KP + (c >> 3) * 8192 + umma::sw128(r, c & 7)) = pack8<__half>(y);
+  if (tid < kPrep) {
+    // =============================================================== prep group
+    // Per iteration k: mask/solve/factors of chunk k, then (while U/W(k) run on the tensor
+    // core) the gates and norms of chunk k+1, then W staging and the hand-over of chunk k.
+    const int wg = tid >> 7;  // column half of the TMEM tiles this thread reads
+    auto chain_item = [&](int chain) -> Item {
+      Item it;
+      it.valid = chain < n_chains;
+      it.first = true;
+      if (!it.valid) return it;
+      it.seq = sorted ? sPerm[chain / p.hv] : chain / p.hv;
+      it.h = chain % p.hv;
+      it.c0 = p.cu[it.seq];
+      it.t_end = p.cu[it.seq + 1];
+      it.n = min(C, it.t_end - it.c0);
+      return it;
+    };
+    // thread 0: the next non-empty chain for this CTA (>= n_chains when none is left)
+    int rr = 0;
+    bool exhausted = false;
+    auto fetch = [&]() -> int {
+      for (;;) {
+        const int c = p.work ? atomicAdd(p.work, 1) : (int)blockIdx.x + (rr++) * (int)gridDim.x;
+        if (c >= n_chains) {
+          exhausted = true;
+          if (p.work && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
+            p.work[0] = 0;
+            p.work[1] = 0;
           }
+          return c;
+        }
+        if (chain_item(c).n > 0) return c;
+      }
+    };
+    // the item after `it` (fetching a new chain when `it` ends one); all prep threads call it
+    int chain = 0;
+    auto next_item = [&](const Item& it) -> Item {
+      if (!it.valid) return it;
+      const bool last = it.c0 + C >= it.t_end;
+      if (last && tid == 0) s_chain = fetch();
+      bar_sync(kBarPrep, kPrep);
+      Item nx = it;
+      if (last) {
+        chain = s_chain;
+        nx = chain_item(chain);
+      } else {
+        nx.c0 += C;
+        nx.n = min(C, nx.t_end - nx.c0);
+        nx.first = false;
+      }
+      bar_sync(kBarPrep, kPrep);  // s_chain may be rewritten by the next call
+      return nx;
+    };
+    // loads issued / consumed (thread 0), for the drain on exit
+    int qk_issued = 0, qk_used = 0, v_issued = 0, v_used = 0;
+    auto issue_qk = [&](const Item& it) {
+      char* dst = sm + SM_QK + (qk_issued & 1) * 32768;
+      uint64_t* bar = &bars.raw_qk[qk_issued & 1];
+      const int kh = it.h / (p.hv / p.hk);
+      tma::expect_tx(bar, 32768);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        tma::load_3d(dst + hh * 16384, &p.tm_q, hh * 64, kh, it.c0, bar);
+        tma::load_3d(dst + hh * 16384 + 8192, &p.tm_k, hh * 64, kh, it.c0, bar);
+      }
+      ++qk_issued;
+    };
+    auto issue_v = [&](const Item& it) {
+      tma::expect_tx(&bars.raw_v, 16384);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) tma::load_3d(sm + SM_V + hh * 8192, &p.tm_v, hh * 64, it.h, it.c0, &bars.raw_v);
+      ++v_issued;
+    };
+    float g_pre = 0.f, b_pre = 0.f;
+    auto load_gates = [&](const Item& it) {
+      if (!it.valid) return;
+      if (tid < C) {
+        g_pre = tid < it.n ? ldg_f(p.g, (int64_t)(it.c0 + tid) * p.sg_t + it.h * p.sg_h, p.g32, kBf16) : 0.f;
+      } else if (tid < 2 * C) {
+        const int r = tid - C;
+        b_pre = r < it.n ? ldg_f(p.beta, (int64_t)(it.c0 + r) * p.sb_t + it.h * p.sb_h, p.b32, kBf16) : 0.f;
+      }
+    };
+    bool ok = true;
+
+    // gates of chunk kk (g_pre/b_pre hold them) -> G, beta, beta e^G; starts the loads of the
+    // gates of `ahead`; publishes e^{G_last} for rec
+    auto gates = [&](int kk, const Item& ahead) {
+      if (tid < C) sF[F_GRAW + tid] = g_pre;
+      else if (tid < 2 * C) sF[F_BRAW + tid - C] = b_pre;
+      bar_sync(kBarPrep, kPrep);
+      load_gates(ahead);
+      if (warp == 0) {
+        const float g0 = sF[F_GRAW + 2 * lane], g1 = sF[F_GRAW + 2 * lane + 1];
+        float incl = g0 + g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const float G0 = (incl - g1) * LOG2E, G1 = incl * LOG2E;
+        const float b0 = sF[F_BRAW + 2 * lane], b1 = sF[F_BRAW + 2 * lane + 1];
+        const float eg0 = exp2f(G0), eg1 = exp2f(G1);
+        sF[F_G + 2 * lane] = G0;
+        sF[F_G + 2 * lane + 1] = G1;
+        sF[F_B + 2 * lane] = b0;
+        sF[F_B + 2 * lane + 1] = b1;
+        sF[F_BW + 2 * lane] = b0 * eg0;
+        sF[F_BW + 2 * lane + 1] = b1 * eg1;
+        const float el = __shfl_sync(0xffffffffu, eg1, 31);
+        if (lane == 0) {
+          s_el[kk & 1] = el;
+          tma::arrive(&bars.gready[kk & 1]);
         }
       }
+    };
+    // raw tile of chunk kk landed -> ask for D1 -> q/k norms (and G - log2(1/|k|) per k column)
+    auto norms = [&](int kk) -> bool {
+      bool w = umma::mbar_wait(&bars.raw_qk[kk & 1], (kk >> 1) & 1);
+      if (tid == 0) qk_used = kk + 1;
+      if (!(w = bar_and(kBarPrep, kPrep, w))) return false;
+      if (tid == 0) tma::arrive(&bars.d1_go);
+      const char* qk = sm + SM_QK + (kk & 1) * 32768;
+      const int row = tid >> 1, hh = tid & 1;  // rows 0-63 q, 64-127 k
+      float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c = qq * 4 + i;
-        const uint32_t off = (c >> 3) * 8192 + umma::sw128(r, c & 7);
+      for (int c = 0; c < 8; ++c) {
         float f[8];
-        unpack8<T>(*reinterpret_cast<const uint4*>(sm + SM_STG + 32768 + off), f);
-        *reinterpret_cast<uint4*>(sm + SM_V + off) = pack8<__half>(f);
-      }
-    }
-    umma::fence_async_smem();
-    umma::fence_before();
-    __syncthreads();
-    umma::fence_after();
-    // staging is free: prefetch the next item while this one computes
-    Item nxt = cur;
-    int next_chain = chain;
-    if (last_chunk) {
-      next_chain = s_chain;
-      nxt = chain_item(next_chain);
-    } else {
-      nxt.c0 += C;
-      nxt.n = min(C, nxt.t_end - nxt.c0);
-    }
-    prefetch(nxt);
-
-    // ---- MMA 1: D1 = [q;k] k^T, O1^T = S^T q^T ----
-    if (tid == 0) {
-      const uint32_t id_d1 = umma::idesc_f16(128, 64, false, false);
-      const uint32_t id_o1 = umma::idesc_f16(128, 64, true, false);
+        unpack8<T>(*reinterpret_cast<const uint4*>(qk + hh * 16384 + umma::sw128(row, c)), f);
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
-        const uint64_t a_qk = umma::smem_desc(sbase + SM_QK + koff, 16, 1024);
-        const uint64_t b_k = umma::smem_desc(sbase + SM_QK + 8192 + koff, 16, 1024);
-        umma::mma_f16(tmem + COL_D1, a_qk, b_k, id_d1, ks > 0);
-        const uint64_t a_st = umma::desc_mnmajor(sbase + SM_S, 16384, ks);
-        const uint64_t b_q = umma::smem_desc(sbase + SM_QK + koff, 16, 1024);
-        umma::mma_f16(tmem + COL_O1, a_st, b_q, id_o1, ks > 0);
+        for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
       }
-      umma::commit(&mbar);
-    }
-    mma_wait();
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const float nf = p.l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
+      if (hh == 0) {
+        if (row < 64) {
+          sF[F_QN + row] = nf;
+        } else {
+          sF[F_KN + row - 64] = nf;
+          sF[F_GC + row - 64] = p.l2norm ? sF[F_G + row - 64] + 0.5f * log2f(ss + 1e-6f) : sF[F_G + row - 64];
+        }
+      }
+      return true;
+    };
+    // D1 of chunk kk done -> its record, and rec may build q'/k' from here on
+    auto publish_norms = [&](int kk, const Item& it) -> bool {
+      bool w = umma::mbar_wait(&bars.d1_done, kk & 1);
+      if (!(w = bar_and(kBarPrep, kPrep, w))) return false;
+      umma::fence_after();
+      if (tid == 0) {
+        Rec r;
+        r.seq = it.seq;
+        r.h = it.h;
+        r.c0 = it.c0;
+        r.n = it.n;
+        r.flags = 1 | (it.first ? 2 : 0) | (it.c0 + C >= it.t_end ? 4 : 0);
+        recs[kk & 1] = r;
+        tma::arrive(&bars.normed);
+      }
+      return true;
+    };
 
-    // ---- masks and decay: Aqk (fp16, K-major B operand) and A (fp32 for the solve) ----
-    // d(i, j) = e^{G_i - G_j} along a row by the recurrence d(i, j-1) = d(i, j) e^{g_j},
-    // restarted at d(i, i) = 1: one multiply per entry instead of an exponential.
-    {
-      float v[32];
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
-      umma::tmem_wait_ld();
-      const int i = tl & 63;
-      const bool qrow = tl < 64;
-      const float bi = qrow ? 1.f : sB[i];
-      const int jhi = wg * 32 + 31;
-      float d = i > jhi ? exp2f(sG[i] - sG[jhi]) : 1.f;  // e^{G_i - G_jhi} for rows below the range
-#pragma unroll
-      for (int j = 31; j >= 0; --j) {
-        const int jj = wg * 32 + j;
-        if (jj == i) d = 1.f;
-        const bool keep = qrow ? jj <= i : jj < i;
-        v[j] = keep ? bi * v[j] * d : 0.f;
-        d *= sAL[jj];
+    if (tid == 0) s_chain = fetch();
+    bar_sync(kBarPrep, kPrep);
+    chain = s_chain;
+    Item cur = chain_item(chain);
+    bar_sync(kBarPrep, kPrep);
+    Item nxt = next_item(cur);
+    if (tid == 0 && cur.valid) {
+      tma::prefetch_map(&p.tm_q);
+      tma::prefetch_map(&p.tm_k);
+      tma::prefetch_map(&p.tm_v);
+      issue_qk(cur);
+      issue_v(cur);
+      if (nxt.valid) issue_qk(nxt);
+    }
+    load_gates(cur);
+    if (cur.valid) {
+      gates(0, nxt);
+      ok = norms(0) && publish_norms(0, cur);
+    }
+
+    for (int k = 0; ok; ++k) {
+      if (!cur.valid) {
+        // end of work: rec sees s_end on its next handshake
+        if (tid == 0) {
+          s_end = 1;
+          tma::arrive(&bars.normed);
+          tma::arrive(&bars.d1_go);
+        }
+        break;
       }
-      if (qrow) {
+
+      // ---- mask and decay of the k rows: A (fp32, for the solve) ----
+      // e^{G_i - G_j} / |k_j| = 2^(G_i - Gc_j) with Gc_j = G_j - log2(1/|k_j|) (log2 units);
+      // masked entries may overflow before the select drops them.
+      if (tl >= 64) {
+        float v[32];
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
+        const int i = tl - 64;
+        const float rowf = sF[F_B + i] * sF[F_KN + i];
+        const float gi = sF[F_G + i];
+        float gc[32];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const float4 x = *reinterpret_cast<const float4*>(sF + F_GC + wg * 32 + 4 * m);
+          gc[4 * m] = x.x; gc[4 * m + 1] = x.y; gc[4 * m + 2] = x.z; gc[4 * m + 3] = x.w;
+        }
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float e = ex2(gi - gc[j]);
+          v[j] = wg * 32 + j < i ? rowf * v[j] * e : 0.f;
+        }
+        float* sA = reinterpret_cast<float*>(sm + SM_A);
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+          *reinterpret_cast<float4*>(sA + fidx4(i, wg * 32 + 4 * m)) =
+              make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3]);
+      }
+      bar_sync(kBarPrep, kPrep);
+
+      // ---- Ti = (I + A)^-1 ----
+      solve_tril64(reinterpret_cast<const float*>(sm + SM_A), reinterpret_cast<float*>(sm + SM_T),
+                   reinterpret_cast<float*>(sm + SM_X), tid);
+      if (tid == 0 && k >= 1) ok = umma::mbar_wait(&bars.r4done, (k - 1) & 1);  // Aqk buffer free
+      if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
+
+      // ---- U/W factors split hi + lo in the input type (they overwrite Ti: read all, then
+      //      write); Aqk (fp16) from the q rows of D1 ----
+      {
+        const float* sT = reinterpret_cast<const float*>(sm + SM_T);
+        uint4 fo[2][4];
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+          const int e = tid + it * kPrep;
+          const int i = e >> 3, ch = e & 7;
+          float uh[8], ul[8], wh[8], wl[8];
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int col = ch * 8 + jj;
+            const float t = i >= col ? sT[fidx(i, col)] : 0.f;
+            const float u = t * sF[F_B + col], w = t * sF[F_BW + col] * sF[F_KN + col];
+            uh[jj] = to_f32<T>(from_f32<T>(u));
+            ul[jj] = u - uh[jj];
+            wh[jj] = to_f32<T>(from_f32<T>(w));
+            wl[jj] = w - wh[jj];
+          }
+          fo[it][0] = pack8<T>(uh);
+          fo[it][1] = pack8<T>(ul);
+          fo[it][2] = pack8<T>(wh);
+          fo[it][3] = pack8<T>(wl);
+        }
+        bar_sync(kBarPrep, kPrep);
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+          const int e = tid + it * kPrep;
+          const uint32_t off = umma::sw128(e >> 3, e & 7);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(sm + SM_TF + q * 8192 + off) = fo[it][q];
+        }
+      }
+      if (tl < 64) {
+        float v[32];
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
+        const int i = tl;
+        const float rowf = p.scale * sF[F_QN + i];
+        const float gi = sF[F_G + i];
+        float gc[32];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const float4 x = *reinterpret_cast<const float4*>(sF + F_GC + wg * 32 + 4 * m);
+          gc[4 * m] = x.x; gc[4 * m + 1] = x.y; gc[4 * m + 2] = x.z; gc[4 * m + 3] = x.w;
+        }
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float e = ex2(gi - gc[j]);
+          v[j] = wg * 32 + j <= i ? rowf * v[j] * e : 0.f;
+        }
 #pragma unroll
         for (int cch = 0; cch < 4; ++cch)
           *reinterpret_cast<uint4*>(sm + SM_AQK + umma::sw128(i, wg * 4 + cch)) = pack8<__half>(v + cch * 8);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sA[fidx(i, wg * 32 + j)] = v[j];
       }
-    }
-    __syncthreads();
+      umma::fence_async_smem();
+      umma::fence_before();
+      bar_sync(kBarPrep, kPrep);
 
-    // ---- solve Ti = (I + A)^-1; Tu = Ti diag(beta), Tw = Ti diag(beta e^G) (fp16, K-major) ----
-    solve_tril64(sA, sT, sX, tid);
-    for (int e = tid; e < C * 8; e += kThreads) {
-      const int i = e >> 3, ch = e & 7;
-      float u[8], w[8];
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int col = ch * 8 + jj;
-        const float t = i >= col ? sT[fidx(i, col)] : 0.f;
-        u[jj] = t * sB[col];
-        w[jj] = t * sBW[col];
+      // ---- U^T = v^T (Tu_hi + Tu_lo)^T, W^T = k^T (Tw_hi + Tw_lo)^T (issued by rec) ----
+      if (tid == 0) tma::arrive(&bars.mma2_go);
+
+      // ---- meanwhile: gates and norms of chunk k+1 (once rec has read chunk k's) ----
+      Item nxt2 = nxt;
+      if (tid == 0) ok = umma::mbar_wait(&bars.conv_done, k & 1);  // rec has built q', k'
+      if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
+      if (nxt.valid) {
+        nxt2 = next_item(nxt);
+        gates(k + 1, nxt2);
+        if (!(ok = norms(k + 1))) break;
       }
-      *reinterpret_cast<uint4*>(sm + SM_TU + umma::sw128(i, ch)) = pack8<__half>(u);
-      *reinterpret_cast<uint4*>(sm + SM_TW + umma::sw128(i, ch)) = pack8<__half>(w);
-    }
-    umma::fence_async_smem();
-    __syncthreads();
 
-    // ---- MMA 2: U^T = v^T Tu^T, W^T = k^T Tw^T ----
-    if (tid == 0) {
+      // ---- U/W done: next loads; stage W^T [kdim][tok] (fp16, MN-major B operand) ----
+      ok = umma::mbar_wait(&bars.mma2_done, k & 1);
+      if (tid == 0) v_used = k + 1;
+      if (ok && tid == 0 && k >= 1) ok = umma::mbar_wait(&bars.r3done, (k - 1) & 1);  // W^T buffer free
+      if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
       umma::fence_after();
-      const uint32_t id = umma::idesc_f16(128, 64, true, false);
-#pragma unroll
-      for (int ks = 0; ks < C / 16; ++ks) {
-        const uint64_t b_tu = umma::smem_desc(sbase + SM_TU + ks * 32, 16, 1024);
-        const uint64_t b_tw = umma::smem_desc(sbase + SM_TW + ks * 32, 16, 1024);
-        umma::mma_f16(tmem + COL_U, umma::desc_mnmajor(sbase + SM_V, 8192, ks), b_tu, id, ks > 0);
-        umma::mma_f16(tmem + COL_W, umma::desc_mnmajor(sbase + SM_QK + 8192, 16384, ks), b_tw, id, ks > 0);
+      if (tid == 0) {
+        if (nxt.valid) issue_v(nxt);
+        if (nxt2.valid && nxt.valid) issue_qk(nxt2);
       }
-      umma::commit(&mbar);
-    }
-    mma_wait();
-
-    // ---- stage w (tokens x kdim, K-major B operand) ----
-    {
-      float v[32];
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_W + wg * 32), v);
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_W + wg * 32 + 16), v + 16);
-      umma::tmem_wait_ld();
-      __half* w = reinterpret_cast<__half*>(sm + SM_W);
-      const int d = tl;  // kdim
+      {
+        float v[32];
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_W + wg * 32), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_W + wg * 32 + 16), v + 16);
+        umma::tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int i = wg * 32 + j;  // token
-        w[umma::elem_off(i, d, 8192) >> 1] = __float2half_rn(v[j]);
+        for (int cch = 0; cch < 4; ++cch)
+          *reinterpret_cast<uint4*>(sm + SM_WS + umma::sw128(tl, wg * 4 + cch)) = pack8<__half>(v + cch * 8);
       }
-    }
-    umma::fence_async_smem();
-    umma::fence_before();
-    __syncthreads();
+      umma::fence_async_smem();
+      umma::fence_before();
+      bar_sync(kBarPrep, kPrep);
+      if (tid == 0) tma::arrive(&bars.ready);
 
-    // ---- MMA 3: Vn^T = U^T - S^T W^T ----
+      if (nxt.valid && !(ok = publish_norms(k + 1, nxt))) break;
+      cur = nxt;
+      nxt = nxt2;
+    }
     if (tid == 0) {
+      if (!ok) report_device_error(1);
+      // copies still in flight (only after an abort) land before the CTA exits
+      for (int i = qk_used; i < qk_issued; ++i) umma::mbar_wait(&bars.raw_qk[i & 1], (i >> 1) & 1);
+      for (int i = v_used; i < v_issued; ++i) umma::mbar_wait(&bars.raw_v, i & 1);
+      // an aborted CTA still counts itself out so the work counter is zeroed for the next launch
+      if (p.work && !exhausted && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
+        p.work[0] = 0;
+        p.work[1] = 0;
+      }
+    }
+  } else {
+    // ================================================================ rec group
+    const int rt = tid - kPrep;  // == tl
+    uint32_t ph = 0;             // mma_r parity
+    bool ok = true;
+    float* gstate = nullptr;
+    T* go = static_cast<T*>(p.o);
+    // Thread rt == 0 issues every tensor-core MMA of the CTA, in the order the pipeline
+    // consumes them: U/W(k), D1(k+1), then (after the hand-over of chunk k) Vn/O(k) and
+    // O/S-update(k).  prep asks for its batches with d1_go / mma2_go and waits on d1_done /
+    // mma2_done (separate barriers: D1(k+1) may complete before prep looks at U/W(k)); rec
+    // waits on mma_r.  One issuing thread also orders every TMEM buffer reuse behind its
+    // readers.
+    const uint32_t id_d1 = umma::idesc_f16(128, 64, false, false, false, kBf16);
+    const uint32_t id_uw = umma::idesc_f16(128, 64, true, false, false, kBf16);
+    const uint32_t id_vn = umma::idesc_f16(128, 64, true, true, true);
+    const uint32_t id_sq = umma::idesc_f16(128, 64, true, false);
+    const uint32_t id_o = umma::idesc_f16(128, 64, false, false);
+    const uint32_t id_s = umma::idesc_f16(128, 128, true, false);
+    // D1 of chunk kk once prep asks for it; false at the end of work
+    auto issue_d1 = [&](int kk, bool& have) -> bool {
+      if (!umma::mbar_wait(&bars.d1_go, kk & 1)) return false;
+      have = *reinterpret_cast<volatile int*>(&s_end) == 0;
+      if (!have) return true;
+      if (!umma::mbar_wait(&bars.raw_qk[kk & 1], (kk >> 1) & 1)) return false;
       umma::fence_after();
-      const uint32_t id = umma::idesc_f16(128, 64, true, false, true);
+      const uint32_t qk_a = sbase + SM_QK + (kk & 1) * 32768;
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks) {
-        const uint64_t b_w = umma::smem_desc(sbase + SM_W + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
-        umma::mma_f16(tmem + COL_U, umma::desc_mnmajor(sbase + SM_S, 16384, ks), b_w, id, true);
+        const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
+        umma::mma_f16(tmem + COL_D1, umma::smem_desc(qk_a + koff, 16, 1024),
+                      umma::smem_desc(qk_a + 8192 + koff, 16, 1024), id_d1, ks > 0);
       }
-      umma::commit(&mbar);
-    }
-    mma_wait();
-
-    // ---- stage v_new (tokens x v), scale S by e^{G_last} in TMEM ----
-    {
-      float v[32];
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_U + wg * 32), v);
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_U + wg * 32 + 16), v + 16);
-      umma::tmem_wait_ld();
-      __half* vn = reinterpret_cast<__half*>(sm + SM_VN);
-      const int vc = tl;  // v column
+      umma::commit(&bars.d1_done);
+      return true;
+    };
+    bool have_next = true;
+    if (rt == 0) ok = issue_d1(0, have_next);
+    ok = bar_and(kBarRec, kRec, ok);
+    for (int k = 0; ok; ++k) {
+      const int b = k & 1;
+      // ---- q' = scale e^{G_i} q / |q| and k' = e^{G_last - G_i} k / |k| (fp16) for chunk k,
+      //      from the raw tile while prep masks and solves it; thread = row of [q; k] ----
+      ok = umma::mbar_wait(&bars.normed, k & 1);
+      if (!(ok = bar_and(kBarRec, kRec, ok))) break;
+      if (*reinterpret_cast<volatile int*>(&s_end)) break;
+      {
+        const char* qk = sm + SM_QK + b * 32768;
+        const int i = rt & 63;
+        float sc;
+        if (rt < 64) sc = p.scale * exp2f(sF[F_G + i]) * sF[F_QN + i];
+        else sc = i < recs[b].n ? exp2f(sF[F_G + C - 1] - sF[F_G + i]) * sF[F_KN + i] : 0.f;
+        char* dst = sm + (rt < 64 ? SM_QP : SM_KP);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) vn[umma::elem_off(wg * 32 + j, vc, 8192) >> 1] = __float2half_rn(v[j]);
-      const float eL = exp2f(sG[C - 1]);
+        for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-      for (int cc = 0; cc < 64; cc += 16) {
-        float s16[16];
-        const uint32_t a = umma::taddr(tmem, lane_base, COL_S + wg * 64 + cc);
-        umma::tmem_ld16(a, s16);
-        umma::tmem_wait_ld();
+          for (int c = 0; c < 8; ++c) {
+            float f[8];
+            unpack8<T>(*reinterpret_cast<const uint4*>(qk + hh * 16384 + umma::sw128(rt, c)), f);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) s16[j] *= eL;
-        umma::tmem_st16(a, s16);
+            for (int j = 0; j < 8; ++j) f[j] *= sc;
+            *reinterpret_cast<uint4*>(dst + hh * 8192 + umma::sw128(i, c)) = pack8<__half>(f);
+          }
       }
-      umma::tmem_wait_st();
-    }
-    umma::fence_async_smem();
-    umma::fence_before();
-    __syncthreads();
+      umma::fence_async_smem();
+      bar_sync(kBarRec, kRec);
 
-    // ---- MMA 4: O2^T = Vn^T Aqk^T, S += k'^T Vn ----
-    if (tid == 0) {
+      // ---- U^T = v^T (Tu_hi + Tu_lo)^T, W^T = k^T (Tw_hi + Tw_lo)^T once prep has the factors ----
+      if (rt == 0) {
+        tma::arrive(&bars.conv_done);
+        ok = umma::mbar_wait(&bars.mma2_go, k & 1) && umma::mbar_wait(&bars.raw_v, k & 1);
+        if (ok) {
+          umma::fence_after();
+          const uint32_t qk_a = sbase + SM_QK + b * 32768, tf = sbase + SM_TF;
+#pragma unroll
+          for (int ks = 0; ks < C / 16; ++ks) {
+            const uint64_t a_v = umma::desc_mnmajor(sbase + SM_V, 8192, ks);
+            const uint64_t a_k = umma::desc_mnmajor(qk_a + 8192, 16384, ks);
+            umma::mma_f16(tmem + COL_U + b * 64, a_v, umma::smem_desc(tf + ks * 32, 16, 1024), id_uw, ks > 0);
+            umma::mma_f16(tmem + COL_U + b * 64, a_v, umma::smem_desc(tf + 8192 + ks * 32, 16, 1024), id_uw, true);
+            umma::mma_f16(tmem + COL_W, a_k, umma::smem_desc(tf + 16384 + ks * 32, 16, 1024), id_uw, ks > 0);
+            umma::mma_f16(tmem + COL_W, a_k, umma::smem_desc(tf + 24576 + ks * 32, 16, 1024), id_uw, true);
+          }
+          umma::commit(&bars.mma2_done);
+          // D1 of the next chunk as soon as prep asks (its TMEM tile is free once prep has
+          // taken Aqk(k) out, which precedes the U/W request)
+          if (have_next) ok = issue_d1(k + 1, have_next);
+        }
+      }
+      if (!(ok = bar_and(kBarRec, kRec, ok))) break;
+
+      ok = umma::mbar_wait(&bars.ready, k & 1);
+      if (!(ok = bar_and(kBarRec, kRec, ok))) break;
+      const Rec rec = recs[b];
+
+      // ---- chain start: state -> TMEM (pre-scaled by e^{G_last}) and its fp16 copy ----
+      if (rec.flags & 2) {
+        gstate = p.state + (int64_t)p.state_idx[rec.seq] * p.ss_n + (int64_t)rec.h * p.ss_h;
+        const float el = s_el[b];
+        const float* srow = gstate + (int64_t)tl * p.ss_k;
+#pragma unroll 2
+        for (int cc = 0; cc < D; cc += 16) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            const float4 x = *reinterpret_cast<const float4*>(srow + cc + j);
+            v[j] = x.x; v[j + 1] = x.y; v[j + 2] = x.z; v[j + 3] = x.w;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; j += 8) {
+            const int col = cc + j;
+            *reinterpret_cast<uint4*>(sm + SM_S16 + (col >> 6) * 16384 + umma::sw128(tl, (col >> 3) & 7)) =
+                pack8<__half>(v + j);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= el;
+          umma::tmem_st16(umma::taddr(tmem, lane_base, COL_S + cc), v);
+        }
+        umma::tmem_wait_st();
+        umma::fence_async_smem();
+        umma::fence_before();
+        bar_sync(kBarRec, kRec);
+      }
+
+      // ---- Vn^T = U^T - S^T W^T,  O^T = S^T q'^T ----
+      if (rt == 0) {
+        umma::fence_after();
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint64_t a_s = umma::desc_mnmajor(sbase + SM_S16, 16384, ks);
+          umma::mma_f16(tmem + COL_U + b * 64, a_s, umma::desc_mnmajor(sbase + SM_WS, 8192, ks), id_vn, true);
+          umma::mma_f16(tmem + COL_O, a_s, umma::desc_kmajor(sbase + SM_QP, 64, ks), id_sq, ks > 0);
+        }
+        umma::commit(&bars.r3done);
+        umma::commit(&bars.mma_r);
+      }
+      ok = umma::mbar_wait(&bars.mma_r, ph);
+      ph ^= 1;
+      if (!(ok = bar_and(kBarRec, kRec, ok))) break;
       umma::fence_after();
-      const uint32_t id_o2 = umma::idesc_f16(128, 64, true, false);
-      const uint32_t id_s = umma::idesc_f16(128, 128, true, true);
-#pragma unroll
-      for (int ks = 0; ks < C / 16; ++ks) {
-        const uint64_t a_vn = umma::desc_mnmajor(sbase + SM_VN, 8192, ks);
-        const uint64_t b_aqk = umma::smem_desc(sbase + SM_AQK + ks * 32, 16, 1024);
-        umma::mma_f16(tmem + COL_O2, a_vn, b_aqk, id_o2, ks > 0);
-        umma::mma_f16(tmem + COL_S, umma::desc_mnmajor(sbase + SM_KP, 8192, ks), a_vn, id_s, true);
-      }
-      umma::commit(&mbar);
-    }
-    mma_wait();
 
-    // ---- epilogue: o = scale (e^{G_i} O1 + O2) via a shared tile (16-byte global stores);
-    //      fp16 copy of S (and the final fp32 state) ----
-    {
-      float o1[32], o2[32];
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O1 + wg * 32), o1);
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O1 + wg * 32 + 16), o1 + 16);
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O2 + wg * 32), o2);
-      umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O2 + wg * 32 + 16), o2 + 16);
-      umma::tmem_wait_ld();
-      T* ot = reinterpret_cast<T*>(sm + SM_O);  // [64 tokens][128 v], 2 v-halves of [64][128 B]
-      const int vc = tl;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int i = wg * 32 + j;
-        ot[umma::elem_off(i, vc, 8192) >> 1] = from_f32<T>(p.scale * (sEG[i] * o1[j] + o2[j]));
-      }
+      // ---- stage Vn^T [v][tok] (fp16, K-major) ----
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        float s32[32];
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_S + wg * 64 + half * 32), s32);
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_S + wg * 64 + half * 32 + 16), s32 + 16);
+        float v[32];
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_U + b * 64 + half * 32), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_U + b * 64 + half * 32 + 16), v + 16);
         umma::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          const int col = wg * 64 + half * 32 + j;
-          *reinterpret_cast<uint4*>(sm + SM_S + (col >> 6) * 16384 + umma::sw128(tl, (col >> 3) & 7)) =
-              pack8<__half>(s32 + j);
-        }
-        if (last_chunk) {
-          float* srow = gstate + (int64_t)tl * p.ss_k + wg * 64 + half * 32;
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(srow + j) = make_float4(s32[j], s32[j + 1], s32[j + 2], s32[j + 3]);
-        }
+        for (int cch = 0; cch < 4; ++cch)
+          *reinterpret_cast<uint4*>(sm + SM_VN + umma::sw128(tl, half * 4 + cch)) = pack8<__half>(v + cch * 8);
       }
-      __syncthreads();
-      // o tile -> global, 16 bytes per access
-      for (int e = tid; e < C * 16; e += kThreads) {
+      umma::fence_async_smem();
+      umma::fence_before();
+      bar_sync(kBarRec, kRec);
+
+      // ---- O^T += Vn^T Aqk^T,  S += k'^T Vn ----
+      if (rt == 0) {
+        umma::fence_after();
+#pragma unroll
+        for (int ks = 0; ks < C / 16; ++ks) {
+          const uint64_t vn = umma::desc_kmajor(sbase + SM_VN, 128, ks);
+          umma::mma_f16(tmem + COL_O, vn, umma::desc_kmajor(sbase + SM_AQK, 64, ks), id_o, true);
+          umma::mma_f16(tmem + COL_S, umma::desc_mnmajor(sbase + SM_KP, 8192, ks), vn, id_s, true);
+        }
+        umma::commit(&bars.r4done);
+        umma::commit(&bars.mma_r);
+      }
+      ok = umma::mbar_wait(&bars.mma_r, ph);
+      ph ^= 1;
+      if (!(ok = bar_and(kBarRec, kRec, ok))) break;
+      umma::fence_after();
+
+      // ---- epilogue: o tile; fp16 copy of S and S e^{G_last} for the next chunk, or the
+      //      final state ----
+      T* ot = reinterpret_cast<T*>(sm + SM_O);  // [64 tok][128 v], 2 v-halves of [64][128 B]
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float v[32];
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O + half * 32), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O + half * 32 + 16), v + 16);
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ot[umma::elem_off(half * 32 + j, tl, 8192) >> 1] = from_f32<T>(v[j]);
+      }
+      if (rec.flags & 4) {
+        float* srow = gstate + (int64_t)tl * p.ss_k;
+#pragma unroll 2
+        for (int cc = 0; cc < D; cc += 16) {
+          float v[16];
+          umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_S + cc), v);
+          umma::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *reinterpret_cast<float4*>(srow + cc + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+      } else {
+        const int nb = (k + 1) & 1;
+        ok = umma::mbar_wait(&bars.gready[nb], ((k + 1) >> 1) & 1);
+        const float el = s_el[nb];
+#pragma unroll 2
+        for (int cc = 0; cc < D; cc += 16) {
+          float v[16];
+          const uint32_t a = umma::taddr(tmem, lane_base, COL_S + cc);
+          umma::tmem_ld16(a, v);
+          umma::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j += 8) {
+            const int col = cc + j;
+            *reinterpret_cast<uint4*>(sm + SM_S16 + (col >> 6) * 16384 + umma::sw128(tl, (col >> 3) & 7)) =
+                pack8<__half>(v + j);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= el;
+          umma::tmem_st16(a, v);
+        }
+        umma::tmem_wait_st();
+      }
+      umma::fence_async_smem();
+      umma::fence_before();
+      if (!(ok = bar_and(kBarRec, kRec, ok))) break;
+      for (int e = rt; e < C * 16; e += kRec) {
         const int i = e >> 4, c16 = e & 15;
-        if (i < n) {
+        if (i < rec.n) {
           const uint4 val = *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7));
-          *reinterpret_cast<uint4*>(go + (int64_t)(c0 + i) * p.so_t + (int64_t)h * p.so_h + c16 * 8) = val;
+          *reinterpret_cast<uint4*>(go + (int64_t)(rec.c0 + i) * p.so_t + (int64_t)rec.h * p.so_h + c16 * 8) = val;
         }
       }
     }
-    umma::fence_async_smem();
-    umma::fence_before();
-    __syncthreads();
-    umma::fence_after();
-    if (abort_flag) break;
-
-    chain_start = last_chunk;
-    chain = next_chain;
-    cur = nxt;
+    if (rt == 0) {
+      if (!ok) report_device_error(1);
+      // every MMA issued so far completes before TMEM is freed
+      umma::commit(&bars.mma_all);
+      umma::mbar_wait(&bars.mma_all, 0);
+    }
   }
 
-  // an aborted CTA still counts itself out so the work counter is zeroed for the next launch
-  if (tid == 0 && p.work && !exhausted && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
-    p.work[0] = 0;
-    p.work[1] = 0;
-  }
-  cp_async_wait<0>();
   umma::fence_before();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == 0) {
+    umma::fence_after();
+    umma::tmem_dealloc(tmem, TMEM_COLS);
+  }
 }
 
 }  // namespace
@@ -672,17 +876,27 @@ bool chunk_tc_supported(const mvb_tensor* q, const mvb_tensor* k, const mvb_tens
          (beta->dtype == MVB_F32 || beta->dtype == q->dtype);
 }
 
+// Returns -1 when the TMA descriptors cannot be built (the caller then runs the token-serial
+// kernel), else an MVB status.
 int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
                     const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
                     mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, cudaStream_t st) {
   Params p;
+  memset(&p, 0, sizeof(p));
+  const int64_t T_tok = q->shape[0];
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)C};
+  auto map3 = [&](CUtensorMap* m, const mvb_tensor* t) {
+    const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)t->shape[1], (cuuint64_t)T_tok};
+    const cuuint64_t str[2] = {(cuuint64_t)t->stride[1] * 2, (cuuint64_t)t->stride[0] * 2};
+    return tma::encode(m, q->dtype, 3, t->data, dims, str, box);
+  };
+  if (!map3(&p.tm_q, q) || !map3(&p.tm_k, k) || !map3(&p.tm_v, v)) return -1;
   p.work = work;
-  p.q = q->data; p.k = k->data; p.v = v->data; p.g = g->data; p.beta = beta->data; p.o = o->data;
+  p.g = g->data; p.beta = beta->data; p.o = o->data;
   p.state = static_cast<float*>(state->data);
   p.state_idx = static_cast<const int32_t*>(idx->data);
   p.cu = static_cast<const int32_t*>(cu->data);
-  p.sq_t = q->stride[0]; p.sq_h = q->stride[1]; p.sk_t = k->stride[0]; p.sk_h = k->stride[1];
-  p.sv_t = v->stride[0]; p.sv_h = v->stride[1]; p.so_t = o->stride[0]; p.so_h = o->stride[1];
+  p.so_t = o->stride[0]; p.so_h = o->stride[1];
   p.sg_t = g->stride[0]; p.sg_h = g->stride[1]; p.sb_t = beta->stride[0]; p.sb_h = beta->stride[1];
   p.ss_n = state->stride[0]; p.ss_h = state->stride[1]; p.ss_k = state->stride[2];
   p.n_seqs = (int)n_seqs; p.hk = (int)q->shape[1]; p.hv = (int)v->shape[1];
