@@ -6,15 +6,13 @@
 //   out[t, c] = silu(sum_j w[c, j] xp[t + j, c])        (fp32 accumulation)
 //   conv_state[idx] <- xp[L : L + W - 1]
 //
-// Prefill tiling: each CTA owns one tile of TILE tokens that never crosses a sequence
-// boundary (tiles are numbered per sequence, so the grid is an upper bound
-// ceil(T/TILE) + S and surplus CTAs exit).  The tile holding a sequence's first token
-// is the only reader of its old conv state; it also writes the new state (reading the
-// tail of x directly), so there is no cross-CTA race on conv_state.
-// Fast path (16-bit data, contiguous 16-byte aligned rows): a CTA stages its tile of
-// TILE + W - 1 rows x 1024 channels (history rows from x or, at a sequence start, from
-// conv_state) into shared memory with 16-byte cp.async -- every load of the tile in
-// flight at once -- then each thread runs a register sliding window over 8 channels.
+// Prefill tiling: each CTA owns one tile of tokens that never crosses a sequence boundary
+// (tiles are numbered per sequence, so the grid is an upper bound ceil(T/TILE) + S and
+// surplus CTAs exit).  The tile holding a sequence's first token is the only reader of its
+// old conv state; it also writes the new state (reading the tail of x directly), so there is
+// no cross-CTA race on conv_state.
+// Fast path (16-bit data, contiguous 16-byte aligned rows): conv1d_fwd_pipe_kernel, 64-token
+// tiles, rows streamed through registers in groups of 8 16-byte loads per thread.
 // Generic path (fp32, strided or unaligned): one thread per VEC channels reading rows
 // directly.
 #include "common.cuh"
@@ -194,72 +192,89 @@ __global__ void __launch_bounds__(128) conv1d_fwd_kernel(ConvParams p) {
   }
 }
 
-constexpr int kSmemTile = 16;  // tokens per CTA tile on the fast path
+// Register-pipelined prefill (16-bit data, contiguous 16-byte rows): a CTA owns kPipeTile
+// tokens x 1024 channels, each thread 8 channels; rows stream through registers in groups
+// of kPipeDepth (all loads of a group in flight before its outputs are computed), the token
+// loop stays rolled so the body fits the instruction cache, and the weights of a thread's 8
+// channels arrive as 16-byte vectors when the weight tensor is contiguous [dim, W].
+constexpr int kPipeTile = 64;
+constexpr int kPipeDepth = 8;
 
 template <typename T, typename TW, int W>
-__global__ void __launch_bounds__(128) conv1d_fwd_smem_kernel(ConvParams p) {
-  constexpr int ROWS = kSmemTile + W - 1;
-  __shared__ __align__(16) uint4 tile[ROWS][128];  // [row][16-byte channel group]
+__global__ void __launch_bounds__(128) conv1d_fwd_pipe_kernel(ConvParams p) {
   int seq, pos0;
-  if (!find_tile(p.cu, p.n_seqs, kSmemTile, blockIdx.x, seq, pos0)) return;
-  const int tid = threadIdx.x;
-  const int c0 = (blockIdx.y * 128 + tid) * 8;
-  const bool ok_c = c0 < p.dim;
+  if (!find_tile(p.cu, p.n_seqs, kPipeTile, blockIdx.x, seq, pos0)) return;
+  const int c0 = (blockIdx.y * 128 + threadIdx.x) * 8;
+  if (c0 >= p.dim) return;
   const int start = p.cu[seq];
   const int L = p.cu[seq + 1] - start;
-  const int pend = min(L, pos0 + kSmemTile);
-  const T* x = static_cast<const T*>(p.x);
-  T* st = static_cast<T*>(p.state) + (int64_t)p.idx[seq] * p.ss_n;
-  // rows: tile row r holds xp[pos0 + r]; xp index e < W-1 is state row e, else x[start + e - (W-1)]
-#pragma unroll
-  for (int r = 0; r < ROWS; ++r) {
-    const int e = pos0 + r;
-    const bool in = ok_c && (e < W - 1 || e - (W - 1) < L);
-    const T* src = e < W - 1 ? st + e * p.ss_t + c0 : x + (int64_t)(start + e - (W - 1)) * p.sx_t + c0;
-    cp_async16(&tile[r][tid], in ? src : x, in);
-  }
-  cp_async_commit();
-  float w[W][8];
-  const TW* wp = static_cast<const TW*>(p.w);
-#pragma unroll
-  for (int j = 0; j < W; ++j)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) w[j][i] = ok_c ? to_f32<TW>(wp[(int64_t)(c0 + i) * p.sw_c + j * p.sw_j]) : 0.f;
-  cp_async_wait<0>();
-  if (!ok_c) return;  // no barrier follows: each thread reads only the column it staged
+  const int pend = min(L, pos0 + kPipeTile);
+  const T* x = static_cast<const T*>(p.x) + c0;
+  T* st = static_cast<T*>(p.state) + (int64_t)p.idx[seq] * p.ss_n + c0;
+  T* out = static_cast<T*>(p.out) + c0;
 
-  // new conv state (only the tile holding position 0 reads and writes conv_state)
-  if (pos0 == 0) {
+  float w[W][8];
+  const TW* wp = static_cast<const TW*>(p.w) + (int64_t)c0 * p.sw_c;
+  constexpr int kWv = 16 / sizeof(TW);  // weights per 16-byte vector
+  if (p.sw_j == 1 && p.sw_c == W && (8 * W) % kWv == 0 && (reinterpret_cast<uintptr_t>(wp) & 15) == 0) {
+    TW wl[8 * W];
 #pragma unroll
-    for (int j = 0; j < W - 1; ++j) {
-      const int e = L + j;  // xp index of new state row j
-      uint4 val;
-      if (e < ROWS) val = tile[e][tid];
-      else val = *reinterpret_cast<const uint4*>(x + (int64_t)(start + e - (W - 1)) * p.sx_t + c0);
-      *reinterpret_cast<uint4*>(st + j * p.ss_t + c0) = val;
-    }
+    for (int v = 0; v < 8 * W / kWv; ++v) reinterpret_cast<uint4*>(wl)[v] = reinterpret_cast<const uint4*>(wp)[v];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < W; ++j) w[j][i] = to_f32<TW>(wl[i * W + j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < W; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[j][i] = to_f32<TW>(wp[(int64_t)i * p.sw_c + j * p.sw_j]);
   }
+
+  // window rows xp[pos0 + j], j < W-1 (xp index e < W-1 is state row e, else x[start + e - (W-1)])
   float win[W][8];
 #pragma unroll
-  for (int j = 0; j < W - 1; ++j) unpack8<T>(tile[j][tid], win[j]);
-  T* out = static_cast<T*>(p.out);
+  for (int j = 0; j < W - 1; ++j) {
+    const int e = pos0 + j;
+    const T* src = e < W - 1 ? st + e * p.ss_t : x + (int64_t)(start + e - (W - 1)) * p.sx_t;
+    unpack8<T>(*reinterpret_cast<const uint4*>(src), win[j]);
+  }
+  // new conv state: the tile holding position 0 is the only reader of the old state
+  if (pos0 == 0) {
+    uint4 ns[W - 1];
 #pragma unroll
-  for (int t = 0; t < kSmemTile; ++t) {
-    if (pos0 + t < pend) {
-      unpack8<T>(tile[t + W - 1][tid], win[W - 1]);
-      float acc[8];
+    for (int j = 0; j < W - 1; ++j) {
+      const int e = L + j;
+      ns[j] = *reinterpret_cast<const uint4*>(e < W - 1 ? st + e * p.ss_t : x + (int64_t)(start + e - (W - 1)) * p.sx_t);
+    }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float a = 0.f;
+    for (int j = 0; j < W - 1; ++j) *reinterpret_cast<uint4*>(st + j * p.ss_t) = ns[j];
+  }
+
+#pragma unroll 1
+  for (int t0 = pos0; t0 < pend; t0 += kPipeDepth) {
+    uint4 rows[kPipeDepth];
 #pragma unroll
-        for (int j = 0; j < W; ++j) a += w[j][i] * win[j][i];
-        acc[i] = p.silu ? __fdividef(a, 1.f + __expf(-a)) : a;
+    for (int b = 0; b < kPipeDepth; ++b)
+      if (t0 + b < pend) rows[b] = __ldcs(reinterpret_cast<const uint4*>(x + (int64_t)(start + t0 + b) * p.sx_t));
+#pragma unroll
+    for (int b = 0; b < kPipeDepth; ++b) {
+      if (t0 + b < pend) {
+        unpack8<T>(rows[b], win[W - 1]);
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float a = 0.f;
+#pragma unroll
+          for (int j = 0; j < W; ++j) a += w[j][i] * win[j][i];
+          acc[i] = p.silu ? __fdividef(a, 1.f + __expf(-a)) : a;
+        }
+        __stcs(reinterpret_cast<uint4*>(out + (int64_t)(start + t0 + b) * p.so_t), pack8<T>(acc));
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) win[j][i] = win[j + 1][i];
       }
-      *reinterpret_cast<uint4*>(out + (int64_t)(start + pos0 + t) * p.so_t + c0) = pack8<T>(acc);
-#pragma unroll
-      for (int j = 0; j < W - 1; ++j)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) win[j][i] = win[j + 1][i];
     }
   }
 }
@@ -315,8 +330,8 @@ void launch_w(bool prefill, bool vec8, const ConvParams& p, int64_t T_tokens, cu
   const int chan_blocks = (p.dim + 128 * VEC - 1) / (128 * VEC);
   if (prefill) {
     if (vec8) {
-      dim3 grid((unsigned)((T_tokens + kSmemTile - 1) / kSmemTile + p.n_seqs), chan_blocks);
-      conv1d_fwd_smem_kernel<T, TW, W><<<grid, 128, 0, st>>>(p);
+      dim3 grid((unsigned)((T_tokens + kPipeTile - 1) / kPipeTile + p.n_seqs), chan_blocks);
+      conv1d_fwd_pipe_kernel<T, TW, W><<<grid, 128, 0, st>>>(p);
     } else {
       dim3 grid((unsigned)((T_tokens + p.tile - 1) / p.tile + p.n_seqs), chan_blocks);
       conv1d_fwd_kernel<T, TW, 1, W><<<grid, 128, 0, st>>>(p);
