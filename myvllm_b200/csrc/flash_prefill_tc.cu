@@ -230,14 +230,18 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
 
       const int j0 = j * BN;
       const bool need_mask = (j0 + BN > kv_len) || (p.causal && j0 + BN - 1 > qoff + q0);
-      float mx = -INFINITY;
+      // the scale is positive, so the row maximum is taken on the raw scores and the scale
+      // folds into one FFMA per element; four partial maxima / sums keep the dependent
+      // chains short (each softmax warp is alone on its scheduler)
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        float v = x[c] * p.scale_log2;
-        if (need_mask && (j0 + c >= kv_len || (p.causal && j0 + c > pos))) v = -INFINITY;
-        x[c] = v;
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < BN; ++c)
+          if (j0 + c >= kv_len || (p.causal && j0 + c > pos)) x[c] = -INFINITY;
       }
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], x[c]);
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
       const float m_new = fmaxf(m, mx);
       const bool grow = m_new > m + 8.f;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
@@ -258,20 +262,21 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
         l *= f;
       }
       if (grow) m = m_new;
-      const float base = m == -INFINITY ? 0.f : m;
+      const float nbase = m == -INFINITY ? 0.f : -m;
       if (j >= 2 && !(ok = warp_wait(&bars->p_free[j & 1], ((j - 2) >> 1) & 1))) break;
       char* pb = smem + C::OFF_P + (j & 1) * C::P_BYTES;
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c8 = 0; c8 < BN / 8; ++c8) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          e[i] = ex2(x[c8 * 8 + i] - base);
-          rs += e[i];
+          e[i] = ex2(fmaf(x[c8 * 8 + i], p.scale_log2, nbase));
+          rs4[i & 3] += e[i];
         }
         *reinterpret_cast<uint4*>(pb + (c8 >> 3) * (BM * 128) + sw128(r, c8 & 7)) = pack8<T>(e);
       }
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l += rs;
       fence_async_smem();
       fence_before();
@@ -381,6 +386,7 @@ int launch_fa_tc(const FaParams& p, int dtype, int d, bool paged, int64_t T_q, i
                  cudaStream_t st) {
   if (d != 64 && d != 128 && d != 256) return -1;
   if (dtype != MVB_BF16 && dtype != MVB_F16) return -1;
+  if (!(p.scale_log2 > 0.f)) return -1;  // the softmax folds a positive scale into its FFMA
   // TMA: 16-byte aligned bases and strides; vectorised epilogue: 16-byte output rows
   if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.o)) return -1;
   if (!aligned_stride(p.sq_t) || !aligned_stride(p.sq_h) || !aligned_stride(p.sk_t) || !aligned_stride(p.sk_h) ||
