@@ -386,7 +386,8 @@ def run_c3(args, rank, world, device):
 # ----------------------------------------------------------------------------- c4 ----
 def run_c4(args, rank, world, device):
     """Config 4: one decode step of a 48-layer hybrid stack (36 GDN + 12 gated full
-    attention, hidden 2048, pre-norm + mixer + residual; no MLP/MoE), 128 sequences with
+    attention, hidden 2048, pre-norm + mixer + residual; no MLP/MoE; each mixer's input
+    projections fused into one GEMM, the GDN gates formed in-kernel), 128 sequences with
     context ~U[1024, 32768] in a paged bf16 KV cache (block 256) and fp32 GDN states.
     Heads are tensor-parallel over the ranks with an NCCL all-reduce after every output
     projection; KV heads are replicated past TP 2."""
@@ -412,6 +413,7 @@ def run_c4(args, rank, world, device):
         if kind == "gdn":
             mixer.A_log.data = mixer.A_log.data.float()
             mixer.dt_bias.data = mixer.dt_bias.data.float()
+        mixer.fuse_projections()  # weights are final: one input GEMM per layer
         layers.append((RMSNorm((hidden,), 1e-6, True).to(device, torch.bfloat16), mixer))
     gdn = [m for k, (_, m) in zip(kinds, layers) if k == "gdn"]
     fa = [m for k, (_, m) in zip(kinds, layers) if k == "full"]

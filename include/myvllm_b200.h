@@ -104,6 +104,23 @@ int mvb_fused_recurrent_gdn(const mvb_tensor* q, const mvb_tensor* k, const mvb_
                             const mvb_tensor* recurrent_state_indices, mvb_tensor* o, float scale,
                             int use_qk_l2norm, void* stream);
 
+/* The two GDN entry points above with the gates formed in the kernel from the layer's raw
+ * projections, as GatedDeltaNet does before calling them (m/layers/linear_attention.py:89-90):
+ * a, b [T, Hv] (fp32 or the dtype of q) take the places of g, beta, and
+ *   g = -exp(A_log[h]) * softplus(a + dt_bias[h]),  beta = sigmoid(b) rounded to b's dtype;
+ * A_log, dt_bias [Hv] (fp32 or the dtype of q).  Saves the layer's elementwise gate kernels. */
+int mvb_chunk_gated_delta_rule_gated(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
+                                     const mvb_tensor* a, const mvb_tensor* b, const mvb_tensor* a_log,
+                                     const mvb_tensor* dt_bias, mvb_tensor* recurrent_state,
+                                     const mvb_tensor* recurrent_state_indices, const mvb_tensor* cu_seqlens,
+                                     mvb_tensor* o, float scale, int use_qk_l2norm, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+int mvb_fused_recurrent_gdn_gated(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
+                                  const mvb_tensor* a, const mvb_tensor* b, const mvb_tensor* a_log,
+                                  const mvb_tensor* dt_bias, mvb_tensor* recurrent_state,
+                                  const mvb_tensor* recurrent_state_indices, mvb_tensor* o, float scale,
+                                  int use_qk_l2norm, void* stream);
+
 /* Varlen (optionally causal) attention.  q [T, Hq, D]; k [T, Hkv, D]; v [T, Hkv, Dv];
  * cu_seqlens [S+1]; o [T, Hq, Dv] (dtype of q).  bf16/f16 only. */
 int mvb_flash_attention_prefill(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,

@@ -16,7 +16,10 @@ void set_error(const char* fmt, ...) {
 
 int check_tensor(const mvb_tensor* t, const char* op, const char* name, int ndim) {
   if (t == nullptr) MVB_FAIL(MVB_ERR_ARG, "%s: %s is NULL", op, name);
-  if (t->ndim != ndim) MVB_FAIL(MVB_ERR_ARG, "%s: %s must have %d dims, got %d", op, name, ndim, t->ndim);
+  // ndim < 0: any rank from 1 to 6 (the caller checks the rank it needs)
+  if (ndim < 0 ? (t->ndim < 1 || t->ndim > 6) : t->ndim != ndim)
+    MVB_FAIL(MVB_ERR_ARG, "%s: %s must have %d dims, got %d", op, name, ndim, t->ndim);
+  ndim = t->ndim;
   for (int i = 0; i < ndim; ++i)
     if (t->shape[i] < 0) MVB_FAIL(MVB_ERR_ARG, "%s: %s has a negative extent", op, name);
   if (numel(t) > 0 && t->data == nullptr) MVB_FAIL(MVB_ERR_ARG, "%s: %s has no data pointer", op, name);

@@ -115,6 +115,34 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
   return u;
 }
 
+// Optional raw-gate inputs of the gated delta rule: with alog set, the kernels read the
+// layer's projections a, b where they would read g, beta and form (as the layer does,
+// m/layers/linear_attention.py:89-90)
+//   g    = -exp(A_log[h]) * softplus(a + dt_bias[h])    fp32, softplus threshold 20 as torch
+//   beta = sigmoid(b)                                    rounded to b's dtype, as torch does
+struct GateDev {
+  const void* alog = nullptr;
+  const void* dtb = nullptr;
+  int alog_dt = 0, dtb_dt = 0;
+};
+
+__device__ __forceinline__ float load_scalar(const void* p, int64_t i, int dtype) {
+  if (dtype == MVB_F32) return static_cast<const float*>(p)[i];
+  if (dtype == MVB_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+__device__ __forceinline__ float raw_gate_g(const GateDev& gd, float a, int h) {
+  const float x = a + load_scalar(gd.dtb, h, gd.dtb_dt);
+  const float sp = x > 20.f ? x : log1pf(expf(x));
+  return -expf(load_scalar(gd.alog, h, gd.alog_dt)) * sp;
+}
+__device__ __forceinline__ float raw_gate_beta(float b, int dtype) {
+  const float s = 1.f / (1.f + expf(-b));
+  if (dtype == MVB_BF16) return __bfloat162float(__float2bfloat16_rn(s));
+  if (dtype == MVB_F16) return __half2float(__float2half_rn(s));
+  return s;
+}
+
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
 // Packs two floats into a bf16x2 / f16x2 register (lo in the low half).

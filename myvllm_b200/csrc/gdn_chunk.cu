@@ -19,27 +19,31 @@ int check_gdn(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
               const mvb_tensor* o, int64_t* n_seqs_out);
 int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                   const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx,
-                  const mvb_tensor* cu, mvb_tensor* o, float scale, int l2norm, cudaStream_t st);
+                  const mvb_tensor* cu, mvb_tensor* o, float scale, int l2norm, const GateDev& gd, cudaStream_t st);
+int make_gate_dev(const char* op, const mvb_tensor* a_log, const mvb_tensor* dt_bias, const mvb_tensor* v,
+                  const mvb_tensor* q, GateDev* out);
 bool chunk_tc_supported(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
                         const mvb_tensor* beta, const mvb_tensor* state, const mvb_tensor* o);
 int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
                     const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
-                    mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, cudaStream_t st);
+                    mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, const GateDev& gd,
+                    cudaStream_t st);
 
 int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
               const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
-              mvb_tensor* o, float scale, int l2norm, void* ws, size_t ws_bytes, cudaStream_t st) {
+              mvb_tensor* o, float scale, int l2norm, void* ws, size_t ws_bytes, const GateDev& gd,
+              cudaStream_t st) {
   if (cu == nullptr) MVB_FAIL(MVB_ERR_ARG, "%s: cu_seqlens is NULL", op);
   int64_t n_seqs = 0;
   int rc = check_gdn(op, q, k, v, g, beta, state, idx, cu, o, &n_seqs);
   if (rc) return rc;
   if (!chunk_tc_supported(q, k, v, g, beta, state, o))
-    return run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, st);
+    return run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, gd, st);
   if (n_seqs == 0 || v->shape[1] == 0) return MVB_OK;
   MVB_CHECK_ARG(ws == nullptr || (ws_bytes >= 8 && (reinterpret_cast<uintptr_t>(ws) & 3) == 0),
                 "%s: workspace must be at least 8 bytes, 4-byte aligned", op);
-  rc = launch_chunk_tc(q, k, v, g, beta, state, idx, cu, o, scale, l2norm, n_seqs, static_cast<int*>(ws), st);
-  return rc < 0 ? run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, st) : rc;
+  rc = launch_chunk_tc(q, k, v, g, beta, state, idx, cu, o, scale, l2norm, n_seqs, static_cast<int*>(ws), gd, st);
+  return rc < 0 ? run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, gd, st) : rc;
 }
 
 }  // namespace mvb
@@ -50,6 +54,21 @@ extern "C" int mvb_chunk_gated_delta_rule(const mvb_tensor* q, const mvb_tensor*
                                           mvb_tensor* o, float scale, int use_qk_l2norm, void* workspace,
                                           size_t workspace_bytes, void* stream) {
   return mvb::run_chunk("chunk_gated_delta_rule", q, k, v, g, beta, recurrent_state, recurrent_state_indices,
-                        cu_seqlens, o, scale, use_qk_l2norm, workspace, workspace_bytes,
+                        cu_seqlens, o, scale, use_qk_l2norm, workspace, workspace_bytes, mvb::GateDev{},
+                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mvb_chunk_gated_delta_rule_gated(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
+                                                const mvb_tensor* a, const mvb_tensor* b, const mvb_tensor* a_log,
+                                                const mvb_tensor* dt_bias, mvb_tensor* recurrent_state,
+                                                const mvb_tensor* recurrent_state_indices,
+                                                const mvb_tensor* cu_seqlens, mvb_tensor* o, float scale,
+                                                int use_qk_l2norm, void* workspace, size_t workspace_bytes,
+                                                void* stream) {
+  mvb::GateDev gd;
+  int rc = mvb::make_gate_dev("chunk_gated_delta_rule_gated", a_log, dt_bias, v, q, &gd);
+  if (rc) return rc;
+  return mvb::run_chunk("chunk_gated_delta_rule_gated", q, k, v, a, b, recurrent_state, recurrent_state_indices,
+                        cu_seqlens, o, scale, use_qk_l2norm, workspace, workspace_bytes, gd,
                         static_cast<cudaStream_t>(stream));
 }

@@ -82,6 +82,7 @@ struct Params {
   int* work;  // [next chain, CTAs done] or null
   int n_seqs, hk, hv, l2norm, g32, b32;
   float scale;
+  GateDev gd;  // raw gates (a, b in the g, beta slots) when gd.alog is set
 };
 
 struct Bars {
@@ -352,9 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       if (!it.valid) return;
       if (tid < C) {
         g_pre = tid < it.n ? ldg_f(p.g, (int64_t)(it.c0 + tid) * p.sg_t + it.h * p.sg_h, p.g32, kBf16) : 0.f;
+        if (p.gd.alog != nullptr && tid < it.n) g_pre = raw_gate_g(p.gd, g_pre, it.h);
       } else if (tid < 2 * C) {
         const int r = tid - C;
         b_pre = r < it.n ? ldg_f(p.beta, (int64_t)(it.c0 + r) * p.sb_t + it.h * p.sb_h, p.b32, kBf16) : 0.f;
+        if (p.gd.alog != nullptr && r < it.n) b_pre = raw_gate_beta(b_pre, p.b32 ? MVB_F32 : (kBf16 ? MVB_BF16 : MVB_F16));
       }
     };
     bool ok = true;
@@ -880,7 +883,8 @@ bool chunk_tc_supported(const mvb_tensor* q, const mvb_tensor* k, const mvb_tens
 // kernel), else an MVB status.
 int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
                     const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
-                    mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, cudaStream_t st) {
+                    mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, const GateDev& gd,
+                    cudaStream_t st) {
   Params p;
   memset(&p, 0, sizeof(p));
   const int64_t T_tok = q->shape[0];
@@ -902,6 +906,7 @@ int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* 
   p.n_seqs = (int)n_seqs; p.hk = (int)q->shape[1]; p.hv = (int)v->shape[1];
   p.l2norm = l2norm ? 1 : 0; p.g32 = g->dtype == MVB_F32; p.b32 = beta->dtype == MVB_F32;
   p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
+  p.gd = gd;
   const int chains = (int)(n_seqs * p.hv);
   const int grid = chains < num_sms() ? chains : num_sms();
   if (q->dtype == MVB_BF16) {

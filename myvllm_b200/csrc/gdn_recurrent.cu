@@ -33,6 +33,7 @@ struct RecParams {
   int64_t ss_n, ss_h, ss_k;  // state strides (V stride must be 1)
   int hk, hv, vdim, l2norm, g_dtype, b_dtype;
   float scale;
+  GateDev gd;  // raw gates (a, b in the g, beta slots) when gd.alog is set
 };
 
 // g and beta may each be fp32 or the activation dtype (the reference layer makes g fp32
@@ -99,8 +100,14 @@ __global__ void __launch_bounds__(kThreads) gdn_recurrent_kernel(RecParams p) {
       sv[i] = vv < p.vdim ? to_f32<T>(vp[t * p.sv_t + h * p.sv_h + vv * p.sv_d]) : 0.f;
     }
     if (tid == 0) {
-      s_gb[0] = expf(load_gate(p.g, (int64_t)t * p.sg_t + h * p.sg_h, p.g_dtype));
-      s_gb[1] = load_gate(p.beta, (int64_t)t * p.sb_t + h * p.sb_h, p.b_dtype);
+      float gv = load_gate(p.g, (int64_t)t * p.sg_t + h * p.sg_h, p.g_dtype);
+      float bv = load_gate(p.beta, (int64_t)t * p.sb_t + h * p.sb_h, p.b_dtype);
+      if (p.gd.alog != nullptr) {
+        gv = raw_gate_g(p.gd, gv, h);
+        bv = raw_gate_beta(bv, p.b_dtype);
+      }
+      s_gb[0] = expf(gv);
+      s_gb[1] = bv;
     }
     __syncthreads();
     if (p.l2norm) {
@@ -212,6 +219,24 @@ int dispatch_k(const RecParams& p, int kdim, int n_seqs, cudaStream_t st) {
 
 }  // namespace
 
+// Validates the per-head A_log / dt_bias vectors of the raw-gate entry points.
+int make_gate_dev(const char* op, const mvb_tensor* a_log, const mvb_tensor* dt_bias, const mvb_tensor* v,
+                  const mvb_tensor* q, GateDev* out) {
+  int rc;
+  if ((rc = check_tensor(a_log, op, "A_log", 1)) || (rc = check_tensor(dt_bias, op, "dt_bias", 1))) return rc;
+  const int64_t hv = v->ndim == 3 ? v->shape[1] : -1;
+  MVB_CHECK_ARG(a_log->shape[0] == hv && dt_bias->shape[0] == hv, "%s: A_log and dt_bias must be [Hv]", op);
+  MVB_CHECK_ARG(a_log->stride[0] == 1 && dt_bias->stride[0] == 1, "%s: A_log and dt_bias must be contiguous", op);
+  MVB_CHECK_ARG((a_log->dtype == MVB_F32 || a_log->dtype == q->dtype) &&
+                    (dt_bias->dtype == MVB_F32 || dt_bias->dtype == q->dtype),
+                "%s: A_log and dt_bias must each be float32 or the dtype of q", op);
+  out->alog = a_log->data;
+  out->dtb = dt_bias->data;
+  out->alog_dt = a_log->dtype;
+  out->dtb_dt = dt_bias->dtype;
+  return MVB_OK;
+}
+
 // Argument validation shared by the recurrent and the chunked entry points.  For decode
 // the token axis of q/k/v/g/beta/o is the sequence axis and cu_seqlens is NULL.
 int check_gdn(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
@@ -253,7 +278,7 @@ int check_gdn(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
 
 int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                   const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx,
-                  const mvb_tensor* cu, mvb_tensor* o, float scale, int l2norm, cudaStream_t st) {
+                  const mvb_tensor* cu, mvb_tensor* o, float scale, int l2norm, const GateDev& gd, cudaStream_t st) {
   int64_t n_seqs = 0;
   int rc = check_gdn(op, q, k, v, g, beta, state, idx, cu, o, &n_seqs);
   if (rc) return rc;
@@ -280,6 +305,7 @@ int run_recurrent(const char* op, const mvb_tensor* q, const mvb_tensor* k, cons
 
   p.g_dtype = g->dtype;
   p.b_dtype = beta->dtype;
+  p.gd = gd;
   int r = MVB_OK;
   switch (q->dtype) {
     case MVB_F32: r = dispatch_k<float>(p, kd, n_seqs, st); break;
@@ -298,5 +324,17 @@ extern "C" int mvb_fused_recurrent_gdn(const mvb_tensor* q, const mvb_tensor* k,
                                        const mvb_tensor* recurrent_state_indices, mvb_tensor* o, float scale,
                                        int use_qk_l2norm, void* stream) {
   return mvb::run_recurrent("fused_recurrent_gdn", q, k, v, g, beta, recurrent_state, recurrent_state_indices,
-                            nullptr, o, scale, use_qk_l2norm, static_cast<cudaStream_t>(stream));
+                            nullptr, o, scale, use_qk_l2norm, mvb::GateDev{}, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mvb_fused_recurrent_gdn_gated(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
+                                             const mvb_tensor* a, const mvb_tensor* b, const mvb_tensor* a_log,
+                                             const mvb_tensor* dt_bias, mvb_tensor* recurrent_state,
+                                             const mvb_tensor* recurrent_state_indices, mvb_tensor* o, float scale,
+                                             int use_qk_l2norm, void* stream) {
+  mvb::GateDev gd;
+  int rc = mvb::make_gate_dev("fused_recurrent_gdn_gated", a_log, dt_bias, v, q, &gd);
+  if (rc) return rc;
+  return mvb::run_recurrent("fused_recurrent_gdn_gated", q, k, v, a, b, recurrent_state, recurrent_state_indices,
+                            nullptr, o, scale, use_qk_l2norm, gd, static_cast<cudaStream_t>(stream));
 }

@@ -10,21 +10,28 @@
 namespace mvb {
 namespace {
 
+// Row r of a [T, H, D] tensor (H = 1 for 2-D) sits at (r / H) * s0 + (r % H) * s1.
+struct Rows3 {
+  int64_t s0, s1;
+  __device__ __forceinline__ int64_t at(int64_t r, int h) const { return (r / h) * s0 + (r % h) * s1; }
+};
+
 template <typename T, typename TW, int NV>  // NV = 16-byte vectors per lane
-__global__ void __launch_bounds__(256) rmsnorm_gated_kernel(const T* x, int64_t sx, const T* gate, int64_t sg,
-                                                            const TW* w, T* out, int64_t so, int64_t rows, int d,
-                                                            float eps) {
+__global__ void __launch_bounds__(256) rmsnorm_gated_kernel(const T* x, Rows3 rx, const T* gate, Rows3 rg,
+                                                            const TW* w, T* out, Rows3 ro, int64_t rows, int heads,
+                                                            int d, float eps) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
+  const int64_t ox = rx.at(row, heads), og = rg.at(row, heads), oo = ro.at(row, heads);
   float xv[NV][8], gv[NV][8];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int c = (i * 32 + lane) * 8;
     if (c < d) {
-      unpack8<T>(*reinterpret_cast<const uint4*>(x + row * sx + c), xv[i]);
-      unpack8<T>(*reinterpret_cast<const uint4*>(gate + row * sg + c), gv[i]);
+      unpack8<T>(*reinterpret_cast<const uint4*>(x + ox + c), xv[i]);
+      unpack8<T>(*reinterpret_cast<const uint4*>(gate + og + c), gv[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss += xv[i][j] * xv[i][j];
     }
@@ -38,16 +45,21 @@ __global__ void __launch_bounds__(256) rmsnorm_gated_kernel(const T* x, int64_t 
       float y[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) y[j] = xv[i][j] * r * to_f32<TW>(w[c + j]) * silu(gv[i][j]);
-      *reinterpret_cast<uint4*>(out + row * so + c) = pack8<T>(y);
+      *reinterpret_cast<uint4*>(out + oo + c) = pack8<T>(y);
     }
   }
+}
+
+Rows3 rows3(const mvb_tensor* t) {
+  return t->ndim == 3 ? Rows3{t->stride[0], t->stride[1]} : Rows3{t->stride[0], 0};
 }
 
 template <typename T, typename TW>
 void launch(const mvb_tensor* x, const mvb_tensor* g, const mvb_tensor* w, mvb_tensor* o, float eps,
             cudaStream_t st) {
-  const int64_t rows = x->shape[0];
-  const int d = (int)x->shape[1];
+  const int heads = x->ndim == 3 ? (int)x->shape[1] : 1;
+  const int64_t rows = x->shape[0] * heads;
+  const int d = (int)x->shape[x->ndim - 1];
   const int nv = (d / 8 + 31) / 32;
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   auto xs = static_cast<const T*>(x->data);
@@ -55,7 +67,7 @@ void launch(const mvb_tensor* x, const mvb_tensor* g, const mvb_tensor* w, mvb_t
   auto ws = static_cast<const TW*>(w->data);
   auto os = static_cast<T*>(o->data);
 #define MVB_NORM_CASE(N) \
-  case N: rmsnorm_gated_kernel<T, TW, N><<<blocks, 256, 0, st>>>(xs, x->stride[0], gs, g->stride[0], ws, os, o->stride[0], rows, d, eps); break;
+  case N: rmsnorm_gated_kernel<T, TW, N><<<blocks, 256, 0, st>>>(xs, rows3(x), gs, rows3(g), ws, os, rows3(o), rows, heads, d, eps); break;
   switch (nv) {
     MVB_NORM_CASE(1)
     MVB_NORM_CASE(2)
@@ -66,25 +78,26 @@ void launch(const mvb_tensor* x, const mvb_tensor* g, const mvb_tensor* w, mvb_t
 }
 
 template <typename T, typename TW, int NV>
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const T* x, int64_t sx, T* res, int64_t sr, const TW* w,
-                                                      T* out, int64_t so, int64_t rows, int d, float eps,
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const T* x, Rows3 rx, T* res, Rows3 rr, const TW* w, T* out,
+                                                      Rows3 ro, int64_t rows, int heads, int d, float eps,
                                                       float w_offset) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
+  const int64_t ox = rx.at(row, heads), orr = rr.at(row, heads), oo = ro.at(row, heads);
   float xv[NV][8];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int c = (i * 32 + lane) * 8;
     if (c < d) {
-      unpack8<T>(*reinterpret_cast<const uint4*>(x + row * sx + c), xv[i]);
+      unpack8<T>(*reinterpret_cast<const uint4*>(x + ox + c), xv[i]);
       if (res != nullptr) {
         float r[8];
-        unpack8<T>(*reinterpret_cast<const uint4*>(res + row * sr + c), r);
+        unpack8<T>(*reinterpret_cast<const uint4*>(res + orr + c), r);
 #pragma unroll
         for (int j = 0; j < 8; ++j) xv[i][j] += r[j];
-        *reinterpret_cast<uint4*>(res + row * sr + c) = pack8<T>(xv[i]);
+        *reinterpret_cast<uint4*>(res + orr + c) = pack8<T>(xv[i]);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss += xv[i][j] * xv[i][j];
@@ -99,7 +112,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* x, int64_t sx, T*
       float y[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) y[j] = xv[i][j] * r * (to_f32<TW>(w[c + j]) + w_offset);
-      *reinterpret_cast<uint4*>(out + row * so + c) = pack8<T>(y);
+      *reinterpret_cast<uint4*>(out + oo + c) = pack8<T>(y);
     }
   }
 }
@@ -107,17 +120,18 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* x, int64_t sx, T*
 template <typename T, typename TW>
 void launch_plain(const mvb_tensor* x, mvb_tensor* res, const mvb_tensor* w, mvb_tensor* o, float eps, float w_off,
                   cudaStream_t st) {
-  const int64_t rows = x->shape[0];
-  const int d = (int)x->shape[1];
+  const int heads = x->ndim == 3 ? (int)x->shape[1] : 1;
+  const int64_t rows = x->shape[0] * heads;
+  const int d = (int)x->shape[x->ndim - 1];
   const int nv = (d / 8 + 31) / 32;
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   auto xs = static_cast<const T*>(x->data);
   auto rs = res ? static_cast<T*>(res->data) : nullptr;
-  const int64_t sr = res ? res->stride[0] : 0;
+  const Rows3 rr = res ? rows3(res) : Rows3{0, 0};
   auto ws = static_cast<const TW*>(w->data);
   auto os = static_cast<T*>(o->data);
 #define MVB_NORM_CASE(N) \
-  case N: rmsnorm_kernel<T, TW, N><<<blocks, 256, 0, st>>>(xs, x->stride[0], rs, sr, ws, os, o->stride[0], rows, d, eps, w_off); break;
+  case N: rmsnorm_kernel<T, TW, N><<<blocks, 256, 0, st>>>(xs, rows3(x), rs, rr, ws, os, rows3(o), rows, heads, d, eps, w_off); break;
   switch (nv) {
     MVB_NORM_CASE(1)
     MVB_NORM_CASE(2)
@@ -135,20 +149,24 @@ extern "C" int mvb_rmsnorm_gated(const mvb_tensor* x, const mvb_tensor* gate, co
   using namespace mvb;
   const char* op = "rmsnorm_gated";
   int rc;
-  if ((rc = check_tensor(x, op, "x", 2)) || (rc = check_tensor(gate, op, "gate", 2)) ||
-      (rc = check_tensor(weight, op, "weight", 1)) || (rc = check_tensor(out, op, "out", 2)))
+  if ((rc = check_tensor(x, op, "x", -1)) || (rc = check_tensor(gate, op, "gate", -1)) ||
+      (rc = check_tensor(weight, op, "weight", 1)) || (rc = check_tensor(out, op, "out", -1)))
     return rc;
-  const int64_t n = x->shape[0], d = x->shape[1];
-  MVB_CHECK_ARG(gate->shape[0] == n && gate->shape[1] == d && out->shape[0] == n && out->shape[1] == d &&
-                    weight->shape[0] == d,
-                "%s: x/gate/out must be [N, D] and weight [D]", op);
+  const int nd = x->ndim;
+  MVB_CHECK_ARG((nd == 2 || nd == 3) && gate->ndim == nd && out->ndim == nd, "%s: x/gate/out must be 2-D or 3-D", op);
+  for (int i = 0; i < nd; ++i)
+    MVB_CHECK_ARG(gate->shape[i] == x->shape[i] && out->shape[i] == x->shape[i], "%s: x/gate/out shapes differ", op);
+  const int64_t d = x->shape[nd - 1];
+  const int64_t n = x->shape[0] * (nd == 3 ? x->shape[1] : 1);
+  MVB_CHECK_ARG(weight->shape[0] == d, "%s: weight must be [D]", op);
   MVB_CHECK_ARG(x->dtype == gate->dtype && x->dtype == out->dtype && (x->dtype == MVB_BF16 || x->dtype == MVB_F16),
                 "%s: x/gate/out must share a 16-bit float dtype", op);
   MVB_CHECK_ARG(weight->dtype == MVB_F32 || weight->dtype == x->dtype, "%s: weight dtype", op);
-  MVB_CHECK_SUPPORTED(d % 8 == 0 && d <= 1024 && x->stride[1] == 1 && gate->stride[1] == 1 && out->stride[1] == 1 &&
-                          weight->stride[0] == 1 && x->stride[0] % 8 == 0 && gate->stride[0] % 8 == 0 &&
-                          out->stride[0] % 8 == 0 && aligned16(x->data) && aligned16(gate->data) &&
-                          aligned16(out->data),
+  bool rows_ok = true;
+  for (const mvb_tensor* t : {x, gate, static_cast<const mvb_tensor*>(out)})
+    rows_ok = rows_ok && t->stride[nd - 1] == 1 && t->stride[0] % 8 == 0 && (nd == 2 || t->stride[1] % 8 == 0) &&
+              aligned16(t->data);
+  MVB_CHECK_SUPPORTED(d % 8 == 0 && d <= 1024 && weight->stride[0] == 1 && rows_ok,
                       "%s: needs D %% 8 == 0, D <= 1024, contiguous 16-byte aligned rows", op);
   if (n == 0) return MVB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -169,23 +187,28 @@ extern "C" int mvb_rmsnorm(const mvb_tensor* x, mvb_tensor* residual, const mvb_
   using namespace mvb;
   const char* op = "rmsnorm";
   int rc;
-  if ((rc = check_tensor(x, op, "x", 2)) || (rc = check_tensor(weight, op, "weight", 1)) ||
-      (rc = check_tensor(out, op, "out", 2)) || (residual && (rc = check_tensor(residual, op, "residual", 2))))
+  if ((rc = check_tensor(x, op, "x", -1)) || (rc = check_tensor(weight, op, "weight", 1)) ||
+      (rc = check_tensor(out, op, "out", -1)) || (residual && (rc = check_tensor(residual, op, "residual", -1))))
     return rc;
-  const int64_t n = x->shape[0], d = x->shape[1];
-  MVB_CHECK_ARG(out->shape[0] == n && out->shape[1] == d && weight->shape[0] == d &&
-                    (!residual || (residual->shape[0] == n && residual->shape[1] == d)),
-                "%s: x/out/residual must be [N, D] and weight [D]", op);
+  const int nd = x->ndim;
+  MVB_CHECK_ARG((nd == 2 || nd == 3) && out->ndim == nd && (!residual || residual->ndim == nd),
+                "%s: x/out/residual must be 2-D or 3-D", op);
+  for (int i = 0; i < nd; ++i)
+    MVB_CHECK_ARG(out->shape[i] == x->shape[i] && (!residual || residual->shape[i] == x->shape[i]),
+                  "%s: x/out/residual shapes differ", op);
+  const int64_t d = x->shape[nd - 1];
+  const int64_t n = x->shape[0] * (nd == 3 ? x->shape[1] : 1);
+  MVB_CHECK_ARG(weight->shape[0] == d, "%s: weight must be [D]", op);
   MVB_CHECK_ARG(x->dtype == out->dtype && (!residual || residual->dtype == x->dtype) &&
                     (x->dtype == MVB_BF16 || x->dtype == MVB_F16),
                 "%s: x/out/residual must share a 16-bit float dtype", op);
   MVB_CHECK_ARG(weight->dtype == MVB_F32 || weight->dtype == x->dtype, "%s: weight dtype", op);
   const int nv = (int)((d / 8 + 31) / 32);
-  MVB_CHECK_SUPPORTED(d % 8 == 0 && (nv == 1 || nv == 2 || nv == 4 || nv == 8) && x->stride[1] == 1 &&
-                          out->stride[1] == 1 && weight->stride[0] == 1 && x->stride[0] % 8 == 0 &&
-                          out->stride[0] % 8 == 0 && aligned16(x->data) && aligned16(out->data) &&
-                          (!residual || (residual->stride[1] == 1 && residual->stride[0] % 8 == 0 &&
-                                         aligned16(residual->data))),
+  bool rows_ok = true;
+  for (const mvb_tensor* t : {x, static_cast<const mvb_tensor*>(out), static_cast<const mvb_tensor*>(residual)})
+    if (t) rows_ok = rows_ok && t->stride[nd - 1] == 1 && t->stride[0] % 8 == 0 && (nd == 2 || t->stride[1] % 8 == 0) &&
+                     aligned16(t->data);
+  MVB_CHECK_SUPPORTED(d % 8 == 0 && (nv == 1 || nv == 2 || nv == 4 || nv == 8) && weight->stride[0] == 1 && rows_ok,
                       "%s: needs D %% 8 == 0, D <= 2048, contiguous 16-byte aligned rows", op);
   if (n == 0) return MVB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

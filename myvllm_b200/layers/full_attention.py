@@ -21,6 +21,7 @@ attributes the caller points at its paged cache ``[n_blocks, block_size, Hkv_ran
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
 from torch import nn
 
 from ..ops.full_attention import flash_attention_prefill, paged_flash_attention_decode, paged_flash_attention_prefill
@@ -58,15 +59,28 @@ class GatedAttention(nn.Module):
     def k_nrom(self):  # the reference's attribute name (m/layers/full_attention.py:47)
         return self.k_norm
 
+    def fuse_projections(self) -> None:
+        """Concatenate q (with its gate), k and v projections of this rank into one weight
+        (and bias), so a forward runs one GEMM instead of three.  Call after the weights are
+        loaded; re-run after changing them."""
+        mods = [self.q_proj, self.k_proj, self.v_proj]
+        self._w_qkv = torch.cat([m.weight.detach() for m in mods], 0)
+        self._b_qkv = torch.cat([m.bias.detach() for m in mods], 0) if self.attention_bias else None
+        self._qkv_split = [m.weight.shape[0] for m in mods]
+
     def forward(self, x: torch.Tensor, rotary_pos_emb_cos: torch.Tensor | None,
                 rotary_pos_emb_sin: torch.Tensor | None) -> torch.Tensor:
         ctx = get_context()
         T = x.size(0)
         D, Dv = self.qk_head_dim, self.v_head_dim
-        q, gate = torch.chunk(self.q_proj(x).view(T, self.num_q_heads, 2 * D), 2, dim=-1)
+        if getattr(self, "_w_qkv", None) is not None:
+            qg, kp, vp = F.linear(x, self._w_qkv, self._b_qkv).split(self._qkv_split, dim=-1)
+        else:
+            qg, kp, vp = self.q_proj(x), self.k_proj(x), self.v_proj(x)
+        q, gate = torch.chunk(qg.view(T, self.num_q_heads, 2 * D), 2, dim=-1)
         q = self.q_norm(q)
-        k = self.k_norm(self.k_proj(x).view(T, self.num_kv_heads, D))
-        v = self.v_proj(x).view(T, self.num_kv_heads, Dv)
+        k = self.k_norm(kp.view(T, self.num_kv_heads, D))
+        v = vp.view(T, self.num_kv_heads, Dv)
         if rotary_pos_emb_cos is not None and rotary_pos_emb_sin is not None:
             q = apply_partial_rotary(q, rotary_pos_emb_cos, rotary_pos_emb_sin)
             k = apply_partial_rotary(k, rotary_pos_emb_cos, rotary_pos_emb_sin)

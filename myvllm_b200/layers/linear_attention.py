@@ -65,16 +65,30 @@ class GatedDeltaNet(nn.Module):
         self.conv_state: torch.Tensor = torch.empty(0)
 
     def gates(self, a: torch.Tensor, b: torch.Tensor):
+        """The layer's gate math in torch (the kernels form the same gates in-kernel from
+        ``gate_inputs``; this is kept for callers of the unfused ops)."""
         beta = b.sigmoid()
         g = -self.A_log.float().exp() * F.softplus(a.float() + self.dt_bias.float())
         return g, beta
 
+    def fuse_projections(self) -> None:
+        """Concatenate the four input projections of this rank into one weight, so a forward
+        runs one GEMM instead of four.  Call after the weights are loaded (like vLLM's
+        post-load weight processing); the forward then slices q|k|v, z, a, b out of one
+        output without copies.  Re-run after changing the projection weights."""
+        ws = [self.in_proj_qkv.weight, self.in_proj_z.weight, self.in_proj_a.weight, self.in_proj_b.weight]
+        self._w_in = torch.cat([w.detach() for w in ws], 0)
+        self._in_split = [w.shape[0] for w in ws]
+
     def forward(self, x: torch.Tensor, cu_seqlens: torch.Tensor, conv_state_indices: torch.Tensor,
                 recurrent_state_indices: torch.Tensor, is_prefill: bool) -> torch.Tensor:
         T = x.shape[0]
-        qkv = self.in_proj_qkv(x)
-        z = self.in_proj_z(x)
-        g, beta = self.gates(self.in_proj_a(x), self.in_proj_b(x))
+        if getattr(self, "_w_in", None) is not None:
+            qkv, z, a, b = F.linear(x, self._w_in).split(self._in_split, dim=-1)
+        else:
+            qkv, z = self.in_proj_qkv(x), self.in_proj_z(x)
+            a, b = self.in_proj_a(x), self.in_proj_b(x)
+        gate_inputs = (a, b, self.A_log, self.dt_bias)  # g, beta are formed inside the kernel
         if is_prefill:
             qkv = causal_conv1d_fn(qkv, self.conv1d.weight, self.conv_state, conv_state_indices, cu_seqlens)
         else:
@@ -84,10 +98,10 @@ class GatedDeltaNet(nn.Module):
         k = k.view(T, self.num_k_heads, self.k_head_dim)
         v = v.view(T, self.num_v_heads, self.v_head_dim)
         if is_prefill:
-            o = chunk_gated_delta_rule(q, k, v, g, beta, self.recurrent_state, recurrent_state_indices, cu_seqlens,
-                                       use_qk_l2norm_in_kernel=True)
+            o = chunk_gated_delta_rule(q, k, v, None, None, self.recurrent_state, recurrent_state_indices, cu_seqlens,
+                                       use_qk_l2norm_in_kernel=True, gate_inputs=gate_inputs)
         else:
-            o = recurrent_gated_delta_rule(q, k, v, g, beta, self.recurrent_state, recurrent_state_indices,
-                                           use_qk_l2norm_in_kernel=True)
+            o = recurrent_gated_delta_rule(q, k, v, None, None, self.recurrent_state, recurrent_state_indices,
+                                           use_qk_l2norm_in_kernel=True, gate_inputs=gate_inputs)
         o = self.norm(o, z.view(T, self.num_v_heads, self.v_head_dim))
         return self.out_proj(o.reshape(T, self.v_size))

@@ -42,6 +42,8 @@ class RMSNorm(nn.Module):
         otherwise (CPU tensors, fp32)."""
         d = x.shape[-1]
         xs = _rows(x)
+        if xs is None and x.dim() == 3 and x.stride(-1) == 1 and residual is None:
+            xs = x  # [T, H, D] with two row strides (e.g. a head view of a fused projection)
         if x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and d % 8 == 0 and d <= 2048 and \
                 xs is not None and (residual is None or residual.is_contiguous()):
             out = torch.empty(xs.shape, dtype=x.dtype, device=x.device)
@@ -77,10 +79,14 @@ class RMSNormGated(nn.Module):
         self.variance_epsilon = eps
 
     def forward(self, x: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+        """x, gate [..., D]; a [T, H, D] gate may be a strided view (e.g. a column slice of a
+        fused projection) -- the kernel takes two row strides, so it is not copied."""
         _lib.require_cuda("RMSNormGated", x, gate, self.weight)
         d = x.shape[-1]
-        xs = x.reshape(-1, d)
-        gs = gate.reshape(-1, d)
+        if x.dim() == 3 and gate.dim() == 3:
+            xs, gs = x, gate
+        else:
+            xs, gs = x.reshape(-1, d), gate.reshape(-1, d)
         out = torch.empty(xs.shape, dtype=x.dtype, device=x.device)
         _lib.call("RMSNormGated", "mvb_rmsnorm_gated", _lib.desc(xs), _lib.desc(gs), _lib.desc(self.weight.detach()),
                   float(self.variance_epsilon), _lib.desc(out), _lib.stream_of(x))

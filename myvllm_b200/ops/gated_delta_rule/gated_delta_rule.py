@@ -35,27 +35,40 @@ def chunk_gated_delta_rule(
     q: torch.Tensor,  # (total_tokens, num_k_heads, k_head_dim)
     k: torch.Tensor,  # (total_tokens, num_k_heads, k_head_dim)
     v: torch.Tensor,  # (total_tokens, num_v_heads, v_head_dim)
-    g: torch.Tensor,  # (total_tokens, num_v_heads)   natural-log decay
-    beta: torch.Tensor,  # (total_tokens, num_v_heads)
+    g: torch.Tensor | None,  # (total_tokens, num_v_heads)   natural-log decay
+    beta: torch.Tensor | None,  # (total_tokens, num_v_heads)
     recurrent_state: torch.Tensor,  # (max_seq_cnt, num_v_heads, k_head_dim, v_head_dim) fp32, in place
     recurrent_state_indices: torch.Tensor,  # (seq_cnt,)
     cu_seqlens: torch.Tensor,  # (seq_cnt + 1,)
     *,
     use_qk_l2norm_in_kernel: bool = False,
+    gate_inputs: tuple | None = None,
 ) -> torch.Tensor:
     """``use_qk_l2norm_in_kernel`` folds the layer's q/k L2 norm (``linear_attention.py:113-114``)
     into the kernel's tile load; the default keeps the reference contract (q, k normalised
-    by the caller)."""
-    _lib.require_cuda("chunk_gated_delta_rule", q, k, v, g, beta, recurrent_state, recurrent_state_indices,
-                      cu_seqlens)
+    by the caller).  ``gate_inputs=(a, b, A_log, dt_bias)`` (with ``g`` and ``beta`` None)
+    forms the gates in the kernel as the layer does (``linear_attention.py:89-90``)."""
     idx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
     cu = cu_seqlens if cu_seqlens.dtype == torch.int32 else cu_seqlens.int()
     o = torch.empty(v.shape, dtype=v.dtype, device=v.device)
     ws = _lib.workspace(q.device, 8, tag="gdn_chunk")  # work counter of the dynamic scheduler
+    scale = float(k.shape[-1] ** -0.5)
+    if gate_inputs is not None:
+        if g is not None or beta is not None:
+            raise ValueError("chunk_gated_delta_rule: pass either g/beta or gate_inputs, not both")
+        a, b, a_log, dt_bias = gate_inputs
+        _lib.require_cuda("chunk_gated_delta_rule", q, k, v, a, b, a_log, dt_bias, recurrent_state,
+                          recurrent_state_indices, cu_seqlens)
+        _lib.call("chunk_gated_delta_rule", "mvb_chunk_gated_delta_rule_gated", _lib.desc(q), _lib.desc(k),
+                  _lib.desc(v), _lib.desc(a), _lib.desc(b), _lib.desc(a_log), _lib.desc(dt_bias),
+                  _lib.desc(recurrent_state), _lib.desc(idx), _lib.desc(cu), _lib.desc(o), scale,
+                  int(use_qk_l2norm_in_kernel), ws.data_ptr(), ws.numel(), _lib.stream_of(q))
+        return o
+    _lib.require_cuda("chunk_gated_delta_rule", q, k, v, g, beta, recurrent_state, recurrent_state_indices,
+                      cu_seqlens)
     _lib.call("chunk_gated_delta_rule", "mvb_chunk_gated_delta_rule", _lib.desc(q), _lib.desc(k), _lib.desc(v),
               _lib.desc(g), _lib.desc(beta), _lib.desc(recurrent_state), _lib.desc(idx), _lib.desc(cu),
-              _lib.desc(o), float(k.shape[-1] ** -0.5), int(use_qk_l2norm_in_kernel), ws.data_ptr(), ws.numel(),
-              _lib.stream_of(q))
+              _lib.desc(o), scale, int(use_qk_l2norm_in_kernel), ws.data_ptr(), ws.numel(), _lib.stream_of(q))
     return o
 
 
@@ -63,13 +76,14 @@ def recurrent_gated_delta_rule(
     q: torch.Tensor,
     k: torch.Tensor,
     v: torch.Tensor,
-    g: torch.Tensor,
-    beta: torch.Tensor,
+    g: torch.Tensor | None,
+    beta: torch.Tensor | None,
     recurrent_state: torch.Tensor,
     recurrent_state_indices: torch.Tensor,
     *,
     use_qk_l2norm_in_kernel: bool = False,
+    gate_inputs: tuple | None = None,
 ) -> torch.Tensor:
     """Decode: one token per sequence (reference ``gated_delta_rule.py:69-92``)."""
     return fused_recurrent_gdn(q, k, v, g, beta, recurrent_state, recurrent_state_indices,
-                               use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+                               use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel, gate_inputs=gate_inputs)

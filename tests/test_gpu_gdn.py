@@ -208,3 +208,39 @@ def test_chunk_no_device_timeouts():
     from myvllm_b200 import _lib
 
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("prefill", [True, False])
+def test_gated_entry_points_match_torch_gates(prefill):
+    """gate_inputs=(a, b, A_log, dt_bias) forms g and beta in the kernel; the result must equal
+    the same op given the layer's torch-computed gates."""
+    import torch.nn.functional as F
+    from myvllm_b200.ops.gated_delta_rule.gated_delta_rule import chunk_gated_delta_rule, recurrent_gated_delta_rule
+
+    lens = [130, 64, 1, 300] if prefill else [1] * 37
+    T, hk, hv = sum(lens), 4, 8
+    g0 = torch.Generator().manual_seed(11)
+    q = torch.randn(T, hk, 128, generator=g0).to(torch.bfloat16).cuda()
+    k = torch.randn(T, hk, 128, generator=g0).to(torch.bfloat16).cuda()
+    v = torch.randn(T, hv, 128, generator=g0).to(torch.bfloat16).cuda()
+    a = torch.randn(T, hv, generator=g0).to(torch.bfloat16).cuda()
+    b = torch.randn(T, hv, generator=g0).to(torch.bfloat16).cuda()
+    a_log = torch.empty(hv).uniform_(0, 2.77, generator=g0).cuda()
+    dt_bias = (0.1 * torch.randn(hv, generator=g0)).cuda()
+    g = -a_log.exp() * F.softplus(a.float() + dt_bias)
+    beta = b.sigmoid()
+    n = len(lens)
+    st0 = 0.1 * torch.randn(n, hv, 128, 128, generator=g0).cuda()
+    idx = torch.arange(n, dtype=torch.int32, device="cuda")
+    s1, s2 = st0.clone(), st0.clone()
+    if prefill:
+        cu = W.cu_from_lengths(lens, "cuda")
+        o1 = chunk_gated_delta_rule(q, k, v, g, beta, s1, idx, cu, use_qk_l2norm_in_kernel=True)
+        o2 = chunk_gated_delta_rule(q, k, v, None, None, s2, idx, cu, use_qk_l2norm_in_kernel=True,
+                                    gate_inputs=(a, b, a_log, dt_bias))
+    else:
+        o1 = recurrent_gated_delta_rule(q, k, v, g, beta, s1, idx, use_qk_l2norm_in_kernel=True)
+        o2 = recurrent_gated_delta_rule(q, k, v, None, None, s2, idx, use_qk_l2norm_in_kernel=True,
+                                        gate_inputs=(a, b, a_log, dt_bias))
+    assert_close(o2, o1, what="output")
+    assert ((s2 - s1).norm() / s1.norm()).item() < 1e-5

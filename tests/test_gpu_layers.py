@@ -151,3 +151,43 @@ def test_gated_attention_prefill_then_decode_paged():
             hist[s] = (K, V)
             assert_close(out[s:s + 1], ref, what=f"decode step {step} seq {s}")
     reset_context()
+
+
+def test_fused_projections_match_unfused():
+    """fuse_projections(): one GEMM over the concatenated input projections must give the
+    same layer outputs (prefill + decode for GatedDeltaNet, prefill for GatedAttention)."""
+    torch.manual_seed(0)
+    layer = _init(GatedDeltaNet(2048, 16, 32, 128, 128, 4), 7).to(dev, torch.bfloat16)
+    layer.A_log.data = layer.A_log.data.float()
+    layer.dt_bias.data = layer.dt_bias.data.float()
+    outs = []
+    for fused in (False, True):
+        cache = LinearAttentionCache(1, 2, 4, 128, 128, 16, 32, torch.bfloat16, torch.device(dev))
+        layer.conv_state, layer.recurrent_state = cache.layer_states(0)
+        slots = [cache.allocate() for _ in range(2)]
+        idx = torch.tensor(slots, dtype=torch.int32, device=dev)
+        if fused:
+            layer.fuse_projections()
+        g = torch.Generator().manual_seed(8)
+        x = torch.randn(150, 2048, generator=g).to(dev, torch.bfloat16)
+        xd = torch.randn(2, 2048, generator=g).to(dev, torch.bfloat16)
+        cu = W.cu_from_lengths([90, 60], dev)
+        outs.append((layer(x, cu, idx, idx, True), layer(xd, None, idx, idx, False),
+                     cache.recurrent_cache[0, slots].clone()))
+    for a, b in zip(outs[0][:2], outs[1][:2]):
+        assert_close(b, a)
+    assert ((outs[1][2] - outs[0][2]).norm() / outs[0][2].norm()).item() < 1e-3
+
+    attn = _init(GatedAttention(2048, 256, 16, 256, 2, False, 1e-6), 9).to(dev, torch.bfloat16)
+    lens = [200, 33]
+    g = torch.Generator().manual_seed(10)
+    x = torch.randn(sum(lens), 2048, generator=g).to(dev, torch.bfloat16)
+    rope = RotaryEmbedding(64, 10_000_000.0).to(dev)
+    cos, sin = rope.cos_sin(torch.cat([torch.arange(n) for n in lens]).to(dev))
+    cu = W.cu_from_lengths(lens, dev)
+    set_context(True, cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=max(lens), max_seqlen_k=max(lens))
+    o1 = attn(x, cos, sin)
+    attn.fuse_projections()
+    o2 = attn(x, cos, sin)
+    reset_context()
+    assert_close(o2, o1)

@@ -54,3 +54,24 @@ def test_rmsnorm_strided_head_rows():
     out = norm(q)
     qf = q.float()
     assert_close(out, qf * torch.rsqrt(qf.pow(2).mean(-1, keepdim=True) + 1e-6) * 2.0)
+
+
+def test_norms_on_two_stride_head_views():
+    """q/k head views and the z gate of a fused projection: [T, H, D] slices whose rows sit
+    at two strides; the kernels index them directly."""
+    from myvllm_b200.layers.norm import RMSNorm, RMSNormGated
+
+    g = torch.Generator().manual_seed(5)
+    y = torch.randn(37, 12352, generator=g).to(torch.bfloat16).cuda()  # a fused projection output
+    k = y[:, 8192:8704].view(37, 2, 256)  # k heads of the fused projection
+    norm = RMSNorm((256,), 1e-6, True).cuda()
+    kf = k.float()
+    assert_close(norm(k), kf * torch.rsqrt(kf.pow(2).mean(-1, keepdim=True) + 1e-6) * 2.0)
+    z = y[:, 9216:12288].view(37, 24, 128)
+    x = torch.randn(37, 24, 128, generator=g).to(torch.bfloat16).cuda()
+    gated = RMSNormGated((128,), 1e-6).cuda()
+    gated.weight.data.uniform_(0.5, 1.5)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * gated.weight.float() * \
+        torch.nn.functional.silu(z.float())
+    assert_close(gated(x, z), ref)
