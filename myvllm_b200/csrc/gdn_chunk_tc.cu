@@ -655,6 +655,18 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       umma::commit(&bars.d1_done);
       return true;
     };
+    // deferred store of the last output tile (o tile in SM_O; pend_n == 0: nothing pending)
+    int pend_c0 = 0, pend_h = 0, pend_n = 0;
+    auto store_o = [&]() {
+      for (int e = rt; e < C * 16; e += kRec) {
+        const int i = e >> 4, c16 = e & 15;
+        if (i < pend_n) {
+          const uint4 val = *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7));
+          *reinterpret_cast<uint4*>(go + (int64_t)(pend_c0 + i) * p.so_t + (int64_t)pend_h * p.so_h + c16 * 8) = val;
+        }
+      }
+      pend_n = 0;
+    };
     bool have_next = true;
     if (rt == 0) ok = issue_d1(0, have_next);
     ok = bar_and(kBarRec, kRec, ok);
@@ -708,6 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
           if (have_next) ok = issue_d1(k + 1, have_next);
         }
       }
+      store_o();  // the previous chunk's output tile, while thread 0 issues the MMAs above
       if (!(ok = bar_and(kBarRec, kRec, ok))) break;
 
       ok = umma::mbar_wait(&bars.ready, k & 1);
@@ -840,14 +853,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       umma::fence_async_smem();
       umma::fence_before();
       if (!(ok = bar_and(kBarRec, kRec, ok))) break;
-      for (int e = rt; e < C * 16; e += kRec) {
-        const int i = e >> 4, c16 = e & 15;
-        if (i < rec.n) {
-          const uint4 val = *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7));
-          *reinterpret_cast<uint4*>(go + (int64_t)(rec.c0 + i) * p.so_t + (int64_t)rec.h * p.so_h + c16 * 8) = val;
-        }
-      }
+      // the tile goes to HBM in the next chunk's U/W window (SM_O is next written by its Vn
+      // staging, which follows the hand-over of that chunk)
+      pend_c0 = rec.c0;
+      pend_h = rec.h;
+      pend_n = rec.n;
     }
+    if (ok) store_o();
     if (rt == 0) {
       if (!ok) report_device_error(1);
       // every MMA issued so far completes before TMEM is freed
