@@ -181,6 +181,60 @@ def cpu_baseline_c1(budget_s: float = 12.0, seed: int = 0):
     return tokens / spent, tokens, spent, host_threads()
 
 
+def cpu_baseline_c2(budget_s: float = 8.0, seed: int = 0):
+    """The oracle (numpy, fp32) of one config-2 decode step -- conv update + l2norm +
+    recurrent GDN over all 32 heads -- on batches of sequences until ``budget_s`` is spent;
+    returns microseconds per full 256-sequence step (extrapolated), the sample size and the
+    BLAS threads used."""
+    import oracle
+    from myvllm_b200 import workloads as W
+
+    rng = np.random.default_rng(seed)
+    n, spent, batch = 0, 0.0, 16
+    while spent < budget_s and n < 256:
+        x = rng.standard_normal((batch, W.GDN_CH)).astype(np.float32)
+        w = (0.02 * rng.standard_normal((W.GDN_CH, W.GDN_W))).astype(np.float32)
+        cst = rng.standard_normal((batch, W.GDN_W - 1, W.GDN_CH)).astype(np.float32)
+        st = (0.1 * rng.standard_normal((batch, W.GDN_HV, W.GDN_DK, W.GDN_DV))).astype(np.float32)
+        g = -rng.uniform(0.01, 1.0, (batch, W.GDN_HV)).astype(np.float32)
+        beta = rng.uniform(0, 1, (batch, W.GDN_HV)).astype(np.float32)
+        idx = np.arange(batch)
+        t0 = time.perf_counter()
+        qkv = oracle.conv.conv1d_update(x, w, cst, idx, dtype=np.float32)
+        q = qkv[:, :2048].reshape(batch, 16, 128)
+        k = qkv[:, 2048:4096].reshape(batch, 16, 128)
+        v = qkv[:, 4096:].reshape(batch, 32, 128)
+        q = q / np.sqrt((q * q).sum(-1, keepdims=True) + 1e-6)
+        k = k / np.sqrt((k * k).sum(-1, keepdims=True) + 1e-6)
+        oracle.gdn.recurrent_step(q, k, v, g, beta, st, idx, dtype=np.float32)
+        spent += time.perf_counter() - t0
+        n += batch
+    return spent / n * 256 * 1e6, n, spent, host_threads()
+
+
+def cpu_baseline_c3(budget_s: float = 8.0, seed: int = 0):
+    """The oracle (numpy, fp32) of causal varlen attention with the config-3 heads on one
+    sequence of growing length until ``budget_s`` is spent; returns tokens/s of the last
+    (longest) sample and its length.  Per-token cost grows with the length, so the
+    sample length is reported with it."""
+    import oracle
+
+    rng = np.random.default_rng(seed)
+    L, best = 256, None
+    total = 0.0
+    while total < budget_s and L <= 16384:
+        q = rng.standard_normal((L, 16, 256)).astype(np.float32)
+        k = rng.standard_normal((L, 2, 256)).astype(np.float32)
+        v = rng.standard_normal((L, 2, 256)).astype(np.float32)
+        t0 = time.perf_counter()
+        oracle.attention.varlen(q, k, v, np.array([0, L]), 1 / 16, True, dtype=np.float32)
+        dt = time.perf_counter() - t0
+        total += dt
+        best = (L / dt, L, dt)
+        L *= 2
+    return best[0], best[1], best[2], host_threads()
+
+
 def run_c1(args, rank, world, device):
     from myvllm_b200 import workloads as W
     from myvllm_b200.ops.gated_delta_rule.gated_delta_rule import chunk_gated_delta_rule  # noqa: F401
@@ -326,7 +380,13 @@ def run_c2(args, rank, world, device):
     state_bytes = 2 * inp["state"].numel() * 4
     pk, src = peaks()
     gbs = state_bytes / (rec_ms * 1e-3) / 1e9
+    cpu = None
+    if world == 1 and rank == 0:
+        us, n, spent, cores = cpu_baseline_c2()
+        cpu = {"value": us, "unit": "us", "cores": cores, "kind": "port",
+               "sample": f"{n} of 256 sequences (numpy oracle, fp32), {spent:.1f} s, extrapolated to the full step"}
     return {"metric": "decode us/step (GDN layer: conv1d update + recurrent GDN)", "value": ms * 1e3, "unit": "us",
+            "cpu_baseline": cpu,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "c2: 256 seqs, state [256,32,128,128] fp32"},
@@ -372,7 +432,13 @@ def run_c3(args, rank, world, device):
     flops = oracle.attention.varlen_flops(inp["cu"].cpu().numpy(), 16, 256, 256, True)
     pk, src = peaks()
     tf = flops / (fa_ms * 1e-3) / 1e12
-    return {"metric": "prefill tokens/s (full attention: KV write + varlen causal FA)",
+    cpu = None
+    if world == 1 and rank == 0:
+        tps, n, spent, cores = cpu_baseline_c3()
+        cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"one {n}-token sequence with the config-3 heads (numpy oracle, fp32), {spent:.1f} s; "
+                         "per-token cost grows with length, so this understates the CPU time at config-3 lengths"}
+    return {"metric": "prefill tokens/s (full attention: KV write + varlen causal FA)", "cpu_baseline": cpu,
             "value": inp["T"] / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "c3: Hq16/Hkv2/D256 causal, 8 seqs ~U[1024,16384]", "tokens": inp["T"]},
