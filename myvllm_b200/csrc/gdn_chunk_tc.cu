@@ -58,18 +58,23 @@ constexpr uint32_t SM_KP = 98304;       // k' fp16 [64 tok][128 kdim]
 constexpr uint32_t SM_AQK = 114688;     // Aqk fp16 [64][64]
 constexpr uint32_t SM_WS = 122880;      // W^T fp16 [128 kdim][64 tok]
 constexpr uint32_t SM_TF = 139264;      // Tu hi, Tu lo, Tw hi, Tw lo: 4 x [64][64] 16-bit
-constexpr uint32_t SM_A = SM_TF;        //   before that: A fp32 [64][64] (fidx4 layout) and
-constexpr uint32_t SM_T = SM_TF + 16384;  //   Ti fp32 [64][64] (fidx layout)
+constexpr uint32_t SM_A = SM_TF;        //   before that: A (then M) as fp16 hi, lo planes and
+constexpr uint32_t SM_T = SM_TF + 16384;  //   Ti as fp16 hi, lo planes ([64][128 B] each, swizzled)
 constexpr uint32_t SM_VN = 172032;      // Vn^T fp16 [128 v][64 tok]; then the o tile [64 tok][128 v]
 constexpr uint32_t SM_O = SM_VN;
 constexpr uint32_t SM_S16 = 188416;     // S fp16 [128 kdim][128 v] (2 x [128][128 B])
-constexpr uint32_t SM_X = 221184;       // solve scratch, 6 warps x 512 B
-constexpr uint32_t SM_F = 224256;       // small fp32 vectors
-// G (log2 units), beta, beta e^G, 1/|q|, 1/|k|, G - log2(1/|k|) per column, raw gates
-constexpr int F_G = 0, F_B = 64, F_BW = 128, F_QN = 192, F_KN = 256, F_GC = 320, F_GRAW = 384, F_BRAW = 448;
-constexpr uint32_t SM_PERM = SM_F + 512 * 4;
-constexpr uint32_t SMEM_BYTES = SM_PERM + kMaxSort * 4 + 1024;  // + alignment slack
-static_assert(SMEM_BYTES <= 232448 - 512, "shared memory budget");
+constexpr uint32_t SM_AD = 221184;      // the 16x16 diagonal blocks of A in fp32 (4 x [16][kAdPitch])
+constexpr int kAdPitch = 260;           //   block pitch in floats (bank-offset blocks)
+constexpr uint32_t SM_F = 225344;       // small fp32 vectors
+// Per chunk, one set by chunk parity (so that the gates and norms of chunk k+1 can be formed
+// while chunk k's are still read): G (log2 units), beta, beta e^G, 1/|q|, 1/|k|,
+// G - log2(1/|k|) per column.  Then the raw gates of the chunk being formed.
+constexpr int F_G = 0, F_B = 64, F_BW = 128, F_QN = 192, F_KN = 256, F_GC = 320, kFSet = 384;
+constexpr int F_GRAW = 2 * kFSet, F_BRAW = 2 * kFSet + 64;
+constexpr uint32_t SM_PERM = SM_F + (2 * kFSet + 128) * 4;  // chain order, uint16 sequence ids
+constexpr uint32_t SMEM_BYTES = SM_PERM + kMaxSort * 2 + 1024;  // + alignment slack
+static_assert(SMEM_BYTES <= 232448 - 1024, "shared memory budget (with the static barriers)");
+static_assert(SM_AD + 4 * kAdPitch * 4 <= SM_F, "diagonal blocks overlap the vectors");
 
 struct Params {
   CUtensorMap tm_q, tm_k, tm_v;
@@ -87,7 +92,7 @@ struct Params {
 
 struct Bars {
   uint64_t raw_qk[2], raw_v, d1_done, mma2_done, mma_r, ready, gready[2], r3done, r4done;
-  uint64_t d1_go, mma2_go, normed, conv_done, mma_all;
+  uint64_t mma2_go, normed, mma_all, mma_all_prep;
 };
 
 // chunk record handed from prep to rec
@@ -116,14 +121,6 @@ __device__ __forceinline__ bool bar_and(int id, int n, bool v) {
   return r != 0;
 }
 
-// fp32 [64][64] matrices of the solve.  Ti: element (i, j) at i * 64 + (j ^ (i & 31)); A: groups
-// of 4 columns swizzled by row (i * 64 + 4 ((j / 4) ^ (i % 16)) + j % 4) so that rows are
-// written with 16-byte stores.
-__device__ __forceinline__ int fidx(int i, int j) { return i * 64 + (j ^ (i & 31)); }
-__device__ __forceinline__ int fidx4(int i, int j) { return i * 64 + ((((j >> 2) ^ (i & 15))) << 2) + (j & 3); }
-template <bool kA>
-__device__ __forceinline__ int midx(int i, int j) { return kA ? fidx4(i, j) : fidx(i, j); }
-
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -137,76 +134,149 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_
   lo = pack2<__half>(x0 - __half2float(h0), x1 - __half2float(h1));
 }
 
-// A fragment (16x16) of block (bi, bj) of a swizzled fp32 [64][64] matrix, split hi/lo.
-template <bool kA>
-__device__ __forceinline__ void frag_a_split(uint32_t* ah, uint32_t* al, const float* M, int bi, int bj, int lane) {
-  const int r = bi * 16 + (lane >> 2), c = bj * 16 + (lane & 3) * 2;
-  split2(M[midx<kA>(r, c)], M[midx<kA>(r, c + 1)], ah[0], al[0]);
-  split2(M[midx<kA>(r + 8, c)], M[midx<kA>(r + 8, c + 1)], ah[1], al[1]);
-  split2(M[midx<kA>(r, c + 8)], M[midx<kA>(r, c + 9)], ah[2], al[2]);
-  split2(M[midx<kA>(r + 8, c + 8)], M[midx<kA>(r + 8, c + 9)], ah[3], al[3]);
+// Three independent fp32 accumulators of a 16x8 product with fp16 hi/lo operands:
+// hi*hi, hi*lo and lo*hi (~fp32 accurate once summed); independent so that the three
+// mma.sync of one step do not wait on each other.
+struct Acc3 {
+  float h[4] = {0.f, 0.f, 0.f, 0.f}, x[4] = {0.f, 0.f, 0.f, 0.f}, y[4] = {0.f, 0.f, 0.f, 0.f};
+  __device__ __forceinline__ void mma(const uint32_t* ah, const uint32_t* al, const uint32_t* bh, const uint32_t* bl) {
+    mma16816<__half>(h, ah, bh);
+    mma16816<__half>(x, ah, bl);
+    mma16816<__half>(y, al, bh);
+  }
+  __device__ __forceinline__ float operator[](int i) const { return h[i] + (x[i] + y[i]); }
+};
+
+// The solve's 64x64 matrices live as fp16 hi + lo planes (x ~ hi + lo, as split2 rounds it),
+// each [64 rows][128 B] with the 128-byte swizzle, so that mma.sync fragments come straight
+// from ldmatrix.  Element (r, c) of a plane is at sw128(r, c / 8) + 2 (c % 8).
+__device__ __forceinline__ uint32_t poff(int r, int c) { return umma::sw128(r, c >> 3) + ((c & 7) << 1); }
+
+// (x0, x1) -> columns (c, c + 1) of row r of the hi and lo planes (c even).
+__device__ __forceinline__ void st_hl2(char* hi, char* lo, int r, int c, float x0, float x1) {
+  uint32_t h, l;
+  split2(x0, x1, h, l);
+  *reinterpret_cast<uint32_t*>(hi + poff(r, c)) = h;
+  *reinterpret_cast<uint32_t*>(lo + poff(r, c)) = l;
+}
+// 8 floats -> one 16-byte chunk of each plane.
+__device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
+  split2(x[0], x[1], hi.x, lo.x);
+  split2(x[2], x[3], hi.y, lo.y);
+  split2(x[4], x[5], hi.z, lo.z);
+  split2(x[6], x[7], hi.w, lo.w);
+}
+// A fragment (16x16, row-major) of the block at (r0, c0).
+__device__ __forceinline__ void ldsm_a(uint32_t* a, const char* plane, int r0, int c0, int lane) {
+  const int mat = lane >> 3;
+  ldmatrix_x4(a[0], a[1], a[2], a[3], smem_u32(plane + umma::sw128(r0 + (mat & 1) * 8 + (lane & 7), (c0 >> 3) + (mat >> 1))));
+}
+// B fragments of the 16 (k) x 16 (n) block at (r0, c0) stored row-major [k][n]: b[0..1] for
+// columns c0..c0+7, b[2..3] for c0+8..c0+15.
+__device__ __forceinline__ void ldsm_b2(uint32_t* b, const char* plane, int r0, int c0, int lane) {
+  const int mat = lane >> 3;
+  ldmatrix_x4_trans(b[0], b[1], b[2], b[3],
+                    smem_u32(plane + umma::sw128(r0 + (mat & 1) * 8 + (lane & 7), (c0 >> 3) + (mat >> 1))));
+}
+// B fragment of the 16 (k) x 8 (n) block at (r0, c0).
+__device__ __forceinline__ void ldsm_b1(uint32_t* b, const char* plane, int r0, int c0, int lane) {
+  ldmatrix_x2_trans(b[0], b[1], smem_u32(plane + umma::sw128(r0 + ((lane >> 3) & 1) * 8 + (lane & 7), c0 >> 3)));
 }
 
-// acc (16x8) += A B with fp16 hi/lo operands: hi*hi + hi*lo + lo*hi (~fp32 accurate).
-__device__ __forceinline__ void mma3(float* acc, const uint32_t* ah, const uint32_t* al, const uint32_t* bh,
-                                     const uint32_t* bl) {
-  mma16816<__half>(acc, ah, bh);
-  mma16816<__half>(acc, ah, bl);
-  mma16816<__half>(acc, al, bh);
-}
-
-// Ti = (I + A)^-1 for the strictly lower 64x64 A in sA; result (lower part) in sT.  Run by
-// the 256 prep threads.  Diagonal 16x16 blocks by right-looking forward substitution
-// (threads 0-63), then for each block diagonal L = 1, 2, 3 every (block (i, j = i - L),
-// 8-column tile) pair is one warp:
-//   X = sum_{k=j}^{i-1} A_ik T_kj[:, tile],   T_ij[:, tile] = -T_ii X
-// with the products on mma.sync (fp16 hi/lo splitting, fp32 accumulate).
-__device__ __forceinline__ void solve_tril64(const float* sA, float* sT, float* sX, int tid) {
+// Ti = (I + A)^-1 for the strictly lower 64x64 A; run by the 256 prep threads.  In: A as hi/lo
+// planes (a_hi, a_lo) and its four diagonal 16x16 blocks in fp32 (aD).  Out: the lower part of
+// Ti as hi/lo planes (t_hi, t_lo; blocks above the diagonal are left unwritten).  With
+// 16x16 blocks T_ij (i >= j) and M_ik = T_ii A_ik:
+//   R0  T_ii by forward substitution in fp32 (threads 0-63, one column each);
+//   R1  M_ik for the six blocks below the diagonal (one warp each, written over A_ik); the
+//       sub-diagonal warps go on to T_{i,i-1} = -M_{i,i-1} T_{i-1,i-1} from their registers;
+//   R2  T_{j+2,j} = -(M_{j+2,j} T_jj + M_{j+2,j+1} T_{j+1,j});
+//   R3  T_30 = -(M_30 T_00 + M_31 T_10 + M_32 T_20)
+// (T_ij = -T_ii sum_k A_ik T_kj, the block form of forward substitution).  Products run on
+// mma.sync with hi/lo operands and fp32 accumulators (hi*hi + hi*lo + lo*hi): fp32-accurate.
+__device__ __forceinline__ void solve_tril64(char* a_hi, char* a_lo, const float* aD, char* t_hi, char* t_lo,
+                                             int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   if (tid < 64) {
     // right-looking: once x[r] is final it updates every later row, so the dependency
     // chain is 16 steps long instead of sum_r r
-    const int base = (tid >> 4) * 16, c = tid & 15;
+    const int blk = tid >> 4, base = blk * 16, c = tid & 15;
+    const float* ad = aD + blk * kAdPitch;
     float x[16];
 #pragma unroll
     for (int r = 0; r < 16; ++r) x[r] = r == c ? 1.f : 0.f;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
 #pragma unroll
-      for (int r2 = r + 1; r2 < 16; ++r2) x[r2] -= sA[fidx4(base + r2, base + r)] * x[r];
+      for (int r2 = r + 1; r2 < 16; ++r2) x[r2] -= ad[r2 * 16 + r] * x[r];
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) sT[fidx(base + r, base + c)] = x[r];
+    for (int r = 0; r < 16; ++r) {
+      const __half h = __float2half_rn(x[r]);
+      *reinterpret_cast<__half*>(t_hi + poff(base + r, base + c)) = h;
+      *reinterpret_cast<__half*>(t_lo + poff(base + r, base + c)) = __float2half_rn(x[r] - __half2float(h));
+    }
   }
   bar_sync(kBarPrep, kPrep);
-  const int r = lane >> 2, c2 = (lane & 3) * 2;
+  const int g = lane >> 2, q2 = (lane & 3) * 2;  // accumulator row / column pair of this lane
+  if (warp < 6) {
+    const int bi = warp < 3 ? warp + 1 : (warp == 5 ? 3 : warp - 1);
+    const int bk = warp < 3 ? warp : (warp == 3 ? 0 : (warp == 4 ? 1 : 0));
+    uint32_t ah[4], al[4], bh[4], bl[4];
+    ldsm_a(ah, t_hi, bi * 16, bi * 16, lane);
+    ldsm_a(al, t_lo, bi * 16, bi * 16, lane);
+    ldsm_b2(bh, a_hi, bi * 16, bk * 16, lane);
+    ldsm_b2(bl, a_lo, bi * 16, bk * 16, lane);
+    Acc3 m0, m1;
+    m0.mma(ah, al, bh, bl);
+    m1.mma(ah, al, bh + 2, bl + 2);
+    float m[2][4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      m[0][e] = m0[e];
+      m[1][e] = m1[e];
+    }
+    __syncwarp();  // A_ik is read by this warp only; M_ik takes its place
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      st_hl2(a_hi, a_lo, bi * 16 + g, bk * 16 + nt * 8 + q2, m[nt][0], m[nt][1]);
+      st_hl2(a_hi, a_lo, bi * 16 + g + 8, bk * 16 + nt * 8 + q2, m[nt][2], m[nt][3]);
+    }
+    if (warp < 3) {
+      // the accumulators of the two column tiles are the A fragment of M_{i,i-1}
+      split2(m[0][0], m[0][1], ah[0], al[0]);
+      split2(m[0][2], m[0][3], ah[1], al[1]);
+      split2(m[1][0], m[1][1], ah[2], al[2]);
+      split2(m[1][2], m[1][3], ah[3], al[3]);
+      ldsm_b2(bh, t_hi, bk * 16, bk * 16, lane);
+      ldsm_b2(bl, t_lo, bk * 16, bk * 16, lane);
+      Acc3 t0, t1;
+      t0.mma(ah, al, bh, bl);
+      t1.mma(ah, al, bh + 2, bl + 2);
+      st_hl2(t_hi, t_lo, bi * 16 + g, bk * 16 + q2, -t0[0], -t0[1]);
+      st_hl2(t_hi, t_lo, bi * 16 + g + 8, bk * 16 + q2, -t0[2], -t0[3]);
+      st_hl2(t_hi, t_lo, bi * 16 + g, bk * 16 + 8 + q2, -t1[0], -t1[1]);
+      st_hl2(t_hi, t_lo, bi * 16 + g + 8, bk * 16 + 8 + q2, -t1[2], -t1[3]);
+    }
+  }
+  bar_sync(kBarPrep, kPrep);
+  // R2 (warps 0-3: block row j + 2, column tile nt) and R3 (warps 4-5, after a barrier)
 #pragma unroll 1
-  for (int lvl = 1; lvl < 4; ++lvl) {
-    if (warp < 2 * (4 - lvl)) {
-      const int bj = warp >> 1, bi = bj + lvl, nt = warp & 1;
-      float X[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int kb = bj; kb < bi; ++kb) {
+  for (int round = 2; round <= 3; ++round) {
+    const bool mine = round == 2 ? warp < 4 : warp < 2;
+    if (mine) {
+      const int j = round == 2 ? warp >> 1 : 0, nt = warp & 1, bi = round == 2 ? j + 2 : 3;
+      Acc3 acc;
+      for (int kb = j; kb < bi; ++kb) {
         uint32_t ah[4], al[4], bh[2], bl[2];
-        frag_a_split<true>(ah, al, sA, bi, kb, lane);
-        const int k = kb * 16 + c2, n = bj * 16 + nt * 8 + r;
-        split2(sT[fidx(k, n)], sT[fidx(k + 1, n)], bh[0], bl[0]);
-        split2(sT[fidx(k + 8, n)], sT[fidx(k + 9, n)], bh[1], bl[1]);
-        mma3(X, ah, al, bh, bl);
+        ldsm_a(ah, a_hi, bi * 16, kb * 16, lane);
+        ldsm_a(al, a_lo, bi * 16, kb * 16, lane);
+        ldsm_b1(bh, t_hi, kb * 16, j * 16 + nt * 8, lane);
+        ldsm_b1(bl, t_lo, kb * 16, j * 16 + nt * 8, lane);
+        acc.mma(ah, al, bh, bl);
       }
-      // X (16 x 8, accumulator layout) -> per-warp scratch -> B-operand layout
-      float* xs = sX + warp * 128;  // [16][8]
-      xs[r * 8 + c2] = X[0]; xs[r * 8 + c2 + 1] = X[1];
-      xs[(r + 8) * 8 + c2] = X[2]; xs[(r + 8) * 8 + c2 + 1] = X[3];
-      __syncwarp();
-      uint32_t ah[4], al[4], bh[2], bl[2];
-      frag_a_split<false>(ah, al, sT, bi, bi, lane);
-      split2(xs[c2 * 8 + r], xs[(c2 + 1) * 8 + r], bh[0], bl[0]);
-      split2(xs[(c2 + 8) * 8 + r], xs[(c2 + 9) * 8 + r], bh[1], bl[1]);
-      float Y[4] = {0.f, 0.f, 0.f, 0.f};
-      mma3(Y, ah, al, bh, bl);
-      const int rr = bi * 16 + r, cc = bj * 16 + nt * 8 + c2;
-      sT[fidx(rr, cc)] = -Y[0]; sT[fidx(rr, cc + 1)] = -Y[1];
-      sT[fidx(rr + 8, cc)] = -Y[2]; sT[fidx(rr + 8, cc + 1)] = -Y[3];
+      st_hl2(t_hi, t_lo, bi * 16 + g, j * 16 + nt * 8 + q2, -acc[0], -acc[1]);
+      st_hl2(t_hi, t_lo, bi * 16 + g + 8, j * 16 + nt * 8 + q2, -acc[2], -acc[3]);
     }
     bar_sync(kBarPrep, kPrep);
   }
@@ -232,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
   const int lane_base = (warp & 3) * 32;  // TMEM lanes this warp may access
   const int tl = tid & 127;               // TMEM lane owned by this thread
   float* sF = reinterpret_cast<float*>(sm + SM_F);
-  int* sPerm = reinterpret_cast<int*>(sm + SM_PERM);
+  uint16_t* sPerm = reinterpret_cast<uint16_t*>(sm + SM_PERM);
   const uint32_t sbase = smem_u32(sm);
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr float LOG2E = 1.4426950408889634f;
@@ -248,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         const int lj = p.cu[j + 1] - p.cu[j];
         rank += (lj > li) || (lj == li && j < i);
       }
-      sPerm[rank] = i;
+      sPerm[rank] = (uint16_t)i;
     }
   }
   if (tid == 0) {
@@ -256,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       umma::mbar_init(&bars.raw_qk[b], 1);
       umma::mbar_init(&bars.gready[b], 1);
     }
-    for (uint64_t* m : {&bars.d1_go, &bars.mma2_go, &bars.normed, &bars.conv_done, &bars.mma_all})
+    for (uint64_t* m : {&bars.mma2_go, &bars.normed, &bars.mma_all, &bars.mma_all_prep})
       umma::mbar_init(m, 1);
     s_end = 0;
     umma::mbar_init(&bars.raw_v, 1);
@@ -274,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
   umma::fence_after();
   const uint32_t tmem = tmem_slot;
   const int n_chains = S * p.hv;
+  const uint32_t id_d1 = umma::idesc_f16(128, 64, false, false, false, kBf16);
 
   if (tid < kPrep) {
     // =============================================================== prep group
@@ -365,6 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     // gates of chunk kk (g_pre/b_pre hold them) -> G, beta, beta e^G; starts the loads of the
     // gates of `ahead`; publishes e^{G_last} for rec
     auto gates = [&](int kk, const Item& ahead) {
+      float* fs = sF + (kk & 1) * kFSet;
       if (tid < C) sF[F_GRAW + tid] = g_pre;
       else if (tid < 2 * C) sF[F_BRAW + tid - C] = b_pre;
       bar_sync(kBarPrep, kPrep);
@@ -380,12 +452,12 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         const float G0 = (incl - g1) * LOG2E, G1 = incl * LOG2E;
         const float b0 = sF[F_BRAW + 2 * lane], b1 = sF[F_BRAW + 2 * lane + 1];
         const float eg0 = exp2f(G0), eg1 = exp2f(G1);
-        sF[F_G + 2 * lane] = G0;
-        sF[F_G + 2 * lane + 1] = G1;
-        sF[F_B + 2 * lane] = b0;
-        sF[F_B + 2 * lane + 1] = b1;
-        sF[F_BW + 2 * lane] = b0 * eg0;
-        sF[F_BW + 2 * lane + 1] = b1 * eg1;
+        fs[F_G + 2 * lane] = G0;
+        fs[F_G + 2 * lane + 1] = G1;
+        fs[F_B + 2 * lane] = b0;
+        fs[F_B + 2 * lane + 1] = b1;
+        fs[F_BW + 2 * lane] = b0 * eg0;
+        fs[F_BW + 2 * lane + 1] = b1 * eg1;
         const float el = __shfl_sync(0xffffffffu, eg1, 31);
         if (lane == 0) {
           s_el[kk & 1] = el;
@@ -393,13 +465,26 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         }
       }
     };
-    // raw tile of chunk kk landed -> ask for D1 -> q/k norms (and G - log2(1/|k|) per k column)
+    // raw tile of chunk kk landed -> D1 = [q; k] k^T on the tensor core (the D1 tile of chunk
+    // kk-1 has been read: its mask and Aqk precede this call) -> q/k norms (and
+    // G - log2(1/|k|) per k column)
     auto norms = [&](int kk) -> bool {
       bool w = umma::mbar_wait(&bars.raw_qk[kk & 1], (kk >> 1) & 1);
       if (tid == 0) qk_used = kk + 1;
       if (!(w = bar_and(kBarPrep, kPrep, w))) return false;
-      if (tid == 0) tma::arrive(&bars.d1_go);
       const char* qk = sm + SM_QK + (kk & 1) * 32768;
+      if (tid == 0) {
+        umma::fence_after();
+        const uint32_t qk_a = smem_u32(qk);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
+          umma::mma_f16(tmem + COL_D1, umma::smem_desc(qk_a + koff, 16, 1024),
+                        umma::smem_desc(qk_a + 8192 + koff, 16, 1024), id_d1, ks > 0);
+        }
+        umma::commit(&bars.d1_done);
+      }
+      float* fs = sF + (kk & 1) * kFSet;
       const int row = tid >> 1, hh = tid & 1;  // rows 0-63 q, 64-127 k
       float ss = 0.f;
 #pragma unroll
@@ -413,10 +498,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       const float nf = p.l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
       if (hh == 0) {
         if (row < 64) {
-          sF[F_QN + row] = nf;
+          fs[F_QN + row] = nf;
         } else {
-          sF[F_KN + row - 64] = nf;
-          sF[F_GC + row - 64] = p.l2norm ? sF[F_G + row - 64] + 0.5f * log2f(ss + 1e-6f) : sF[F_G + row - 64];
+          fs[F_KN + row - 64] = nf;
+          fs[F_GC + row - 64] = p.l2norm ? fs[F_G + row - 64] + 0.5f * log2f(ss + 1e-6f) : fs[F_G + row - 64];
         }
       }
       return true;
@@ -465,11 +550,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         if (tid == 0) {
           s_end = 1;
           tma::arrive(&bars.normed);
-          tma::arrive(&bars.d1_go);
         }
         break;
       }
 
+      const float* sFk = sF + (k & 1) * kFSet;  // gates and norms of chunk k
       // ---- mask and decay of the k rows: A (fp32, for the solve) ----
       // e^{G_i - G_j} / |k_j| = 2^(G_i - Gc_j) with Gc_j = G_j - log2(1/|k_j|) (log2 units);
       // masked entries may overflow before the select drops them.
@@ -478,12 +563,12 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
         umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
         const int i = tl - 64;
-        const float rowf = sF[F_B + i] * sF[F_KN + i];
-        const float gi = sF[F_G + i];
+        const float rowf = sFk[F_B + i] * sFk[F_KN + i];
+        const float gi = sFk[F_G + i];
         float gc[32];
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
-          const float4 x = *reinterpret_cast<const float4*>(sF + F_GC + wg * 32 + 4 * m);
+          const float4 x = *reinterpret_cast<const float4*>(sFk + F_GC + wg * 32 + 4 * m);
           gc[4 * m] = x.x; gc[4 * m + 1] = x.y; gc[4 * m + 2] = x.z; gc[4 * m + 3] = x.w;
         }
         umma::tmem_wait_ld();
@@ -492,35 +577,50 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
           const float e = ex2(gi - gc[j]);
           v[j] = wg * 32 + j < i ? rowf * v[j] * e : 0.f;
         }
-        float* sA = reinterpret_cast<float*>(sm + SM_A);
 #pragma unroll
-        for (int m = 0; m < 8; ++m)
-          *reinterpret_cast<float4*>(sA + fidx4(i, wg * 32 + 4 * m)) =
-              make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3]);
+        for (int cch = 0; cch < 4; ++cch) {
+          uint4 hi, lo;
+          split8(v + cch * 8, hi, lo);
+          *reinterpret_cast<uint4*>(sm + SM_A + umma::sw128(i, wg * 4 + cch)) = hi;
+          *reinterpret_cast<uint4*>(sm + SM_A + 8192 + umma::sw128(i, wg * 4 + cch)) = lo;
+        }
+        // the diagonal block of row i in fp32 for the forward substitution
+        const int blk = i >> 4;
+        if ((blk >> 1) == wg) {
+          float* ad = reinterpret_cast<float*>(sm + SM_AD) + blk * kAdPitch + (i & 15) * 16;
+          const bool up = blk & 1;  // static register indices only (no local-memory copy of v)
+          float src[16];
+#pragma unroll
+          for (int m = 0; m < 16; ++m) src[m] = up ? v[16 + m] : v[m];
+#pragma unroll
+          for (int m = 0; m < 4; ++m)
+            *reinterpret_cast<float4*>(ad + 4 * m) = make_float4(src[4 * m], src[4 * m + 1], src[4 * m + 2], src[4 * m + 3]);
+        }
       }
       bar_sync(kBarPrep, kPrep);
 
       // ---- Ti = (I + A)^-1 ----
-      solve_tril64(reinterpret_cast<const float*>(sm + SM_A), reinterpret_cast<float*>(sm + SM_T),
-                   reinterpret_cast<float*>(sm + SM_X), tid);
+      solve_tril64(sm + SM_A, sm + SM_A + 8192, reinterpret_cast<const float*>(sm + SM_AD), sm + SM_T,
+                   sm + SM_T + 8192, tid);
       if (tid == 0 && k >= 1) ok = umma::mbar_wait(&bars.r4done, (k - 1) & 1);  // Aqk buffer free
       if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
 
       // ---- U/W factors split hi + lo in the input type (they overwrite Ti: read all, then
       //      write); Aqk (fp16) from the q rows of D1 ----
       {
-        const float* sT = reinterpret_cast<const float*>(sm + SM_T);
         uint4 fo[2][4];
 #pragma unroll
         for (int it = 0; it < 2; ++it) {
           const int e = tid + it * kPrep;
           const int i = e >> 3, ch = e & 7;
-          float uh[8], ul[8], wh[8], wl[8];
+          float uh[8], ul[8], wh[8], wl[8], th[8], tlo[8];
+          unpack8<__half>(*reinterpret_cast<const uint4*>(sm + SM_T + umma::sw128(i, ch)), th);
+          unpack8<__half>(*reinterpret_cast<const uint4*>(sm + SM_T + 8192 + umma::sw128(i, ch)), tlo);
 #pragma unroll
           for (int jj = 0; jj < 8; ++jj) {
             const int col = ch * 8 + jj;
-            const float t = i >= col ? sT[fidx(i, col)] : 0.f;
-            const float u = t * sF[F_B + col], w = t * sF[F_BW + col] * sF[F_KN + col];
+            const float t = i >= col ? th[jj] + tlo[jj] : 0.f;
+            const float u = t * sFk[F_B + col], w = t * sFk[F_BW + col] * sFk[F_KN + col];
             uh[jj] = to_f32<T>(from_f32<T>(u));
             ul[jj] = u - uh[jj];
             wh[jj] = to_f32<T>(from_f32<T>(w));
@@ -545,12 +645,12 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
         umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
         const int i = tl;
-        const float rowf = p.scale * sF[F_QN + i];
-        const float gi = sF[F_G + i];
+        const float rowf = p.scale * sFk[F_QN + i];
+        const float gi = sFk[F_G + i];
         float gc[32];
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
-          const float4 x = *reinterpret_cast<const float4*>(sF + F_GC + wg * 32 + 4 * m);
+          const float4 x = *reinterpret_cast<const float4*>(sFk + F_GC + wg * 32 + 4 * m);
           gc[4 * m] = x.x; gc[4 * m + 1] = x.y; gc[4 * m + 2] = x.z; gc[4 * m + 3] = x.w;
         }
         umma::tmem_wait_ld();
@@ -572,8 +672,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
 
       // ---- meanwhile: gates and norms of chunk k+1 (once rec has read chunk k's) ----
       Item nxt2 = nxt;
-      if (tid == 0) ok = umma::mbar_wait(&bars.conv_done, k & 1);  // rec has built q', k'
-      if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
       if (nxt.valid) {
         nxt2 = next_item(nxt);
         gates(k + 1, nxt2);
@@ -610,7 +708,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     }
     if (tid == 0) {
       if (!ok) report_device_error(1);
-      // copies still in flight (only after an abort) land before the CTA exits
+      // copies and D1 products still in flight (only after an abort) land before the CTA exits
+      umma::commit(&bars.mma_all_prep);
+      umma::mbar_wait(&bars.mma_all_prep, 0);
       for (int i = qk_used; i < qk_issued; ++i) umma::mbar_wait(&bars.raw_qk[i & 1], (i >> 1) & 1);
       for (int i = v_used; i < v_issued; ++i) umma::mbar_wait(&bars.raw_v, i & 1);
       // an aborted CTA still counts itself out so the work counter is zeroed for the next launch
@@ -626,35 +726,15 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     bool ok = true;
     float* gstate = nullptr;
     T* go = static_cast<T*>(p.o);
-    // Thread rt == 0 issues every tensor-core MMA of the CTA, in the order the pipeline
-    // consumes them: U/W(k), D1(k+1), then (after the hand-over of chunk k) Vn/O(k) and
-    // O/S-update(k).  prep asks for its batches with d1_go / mma2_go and waits on d1_done /
-    // mma2_done (separate barriers: D1(k+1) may complete before prep looks at U/W(k)); rec
-    // waits on mma_r.  One issuing thread also orders every TMEM buffer reuse behind its
-    // readers.
-    const uint32_t id_d1 = umma::idesc_f16(128, 64, false, false, false, kBf16);
+    // Thread rt == 0 issues the tensor-core MMAs of the recurrence, in the order the pipeline
+    // consumes them: U/W(k), then (after the hand-over of chunk k) Vn/O(k) and O/S-update(k).
+    // prep asks for U/W with mma2_go and waits on mma2_done; rec waits on mma_r.  (prep's
+    // thread 0 issues the D1 products itself: they use their own TMEM columns.)
     const uint32_t id_uw = umma::idesc_f16(128, 64, true, false, false, kBf16);
     const uint32_t id_vn = umma::idesc_f16(128, 64, true, true, true);
     const uint32_t id_sq = umma::idesc_f16(128, 64, true, false);
     const uint32_t id_o = umma::idesc_f16(128, 64, false, false);
     const uint32_t id_s = umma::idesc_f16(128, 128, true, false);
-    // D1 of chunk kk once prep asks for it; false at the end of work
-    auto issue_d1 = [&](int kk, bool& have) -> bool {
-      if (!umma::mbar_wait(&bars.d1_go, kk & 1)) return false;
-      have = *reinterpret_cast<volatile int*>(&s_end) == 0;
-      if (!have) return true;
-      if (!umma::mbar_wait(&bars.raw_qk[kk & 1], (kk >> 1) & 1)) return false;
-      umma::fence_after();
-      const uint32_t qk_a = sbase + SM_QK + (kk & 1) * 32768;
-#pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
-        umma::mma_f16(tmem + COL_D1, umma::smem_desc(qk_a + koff, 16, 1024),
-                      umma::smem_desc(qk_a + 8192 + koff, 16, 1024), id_d1, ks > 0);
-      }
-      umma::commit(&bars.d1_done);
-      return true;
-    };
     // deferred store of the last output tile (o tile in SM_O; pend_n == 0: nothing pending)
     int pend_c0 = 0, pend_h = 0, pend_n = 0;
     auto store_o = [&]() {
@@ -667,9 +747,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       }
       pend_n = 0;
     };
-    bool have_next = true;
-    if (rt == 0) ok = issue_d1(0, have_next);
-    ok = bar_and(kBarRec, kRec, ok);
     for (int k = 0; ok; ++k) {
       const int b = k & 1;
       // ---- q' = scale e^{G_i} q / |q| and k' = e^{G_last - G_i} k / |k| (fp16) for chunk k,
@@ -681,8 +758,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         const char* qk = sm + SM_QK + b * 32768;
         const int i = rt & 63;
         float sc;
-        if (rt < 64) sc = p.scale * exp2f(sF[F_G + i]) * sF[F_QN + i];
-        else sc = i < recs[b].n ? exp2f(sF[F_G + C - 1] - sF[F_G + i]) * sF[F_KN + i] : 0.f;
+        const float* sFk = sF + b * kFSet;
+        if (rt < 64) sc = p.scale * exp2f(sFk[F_G + i]) * sFk[F_QN + i];
+        else sc = i < recs[b].n ? exp2f(sFk[F_G + C - 1] - sFk[F_G + i]) * sFk[F_KN + i] : 0.f;
         char* dst = sm + (rt < 64 ? SM_QP : SM_KP);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
@@ -700,7 +778,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
 
       // ---- U^T = v^T (Tu_hi + Tu_lo)^T, W^T = k^T (Tw_hi + Tw_lo)^T once prep has the factors ----
       if (rt == 0) {
-        tma::arrive(&bars.conv_done);
         ok = umma::mbar_wait(&bars.mma2_go, k & 1) && umma::mbar_wait(&bars.raw_v, k & 1);
         if (ok) {
           umma::fence_after();
@@ -715,9 +792,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
             umma::mma_f16(tmem + COL_W, a_k, umma::smem_desc(tf + 24576 + ks * 32, 16, 1024), id_uw, true);
           }
           umma::commit(&bars.mma2_done);
-          // D1 of the next chunk as soon as prep asks (its TMEM tile is free once prep has
-          // taken Aqk(k) out, which precedes the U/W request)
-          if (have_next) ok = issue_d1(k + 1, have_next);
         }
       }
       store_o();  // the previous chunk's output tile, while thread 0 issues the MMAs above
