@@ -384,18 +384,17 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     int chain = 0;
     auto next_item = [&](const Item& it) -> Item {
       if (!it.valid) return it;
-      const bool last = it.c0 + C >= it.t_end;
-      if (last && tid == 0) s_chain = fetch();
-      bar_sync(kBarPrep, kPrep);
       Item nx = it;
-      if (last) {
-        chain = s_chain;
-        nx = chain_item(chain);
-      } else {
+      if (it.c0 + C < it.t_end) {  // same chain (uniform across the group: no barrier needed)
         nx.c0 += C;
         nx.n = min(C, nx.t_end - nx.c0);
         nx.first = false;
+        return nx;
       }
+      if (tid == 0) s_chain = fetch();
+      bar_sync(kBarPrep, kPrep);
+      chain = s_chain;
+      nx = chain_item(chain);
       bar_sync(kBarPrep, kPrep);  // s_chain may be rewritten by the next call
       return nx;
     };
