@@ -477,8 +477,9 @@ def run_c4(args, rank, world, device):
     attention, hidden 2048, pre-norm + mixer + residual; no MLP/MoE; each mixer's input
     projections fused into one GEMM, the GDN gates formed in-kernel), 128 sequences with
     context ~U[1024, 32768] in a paged bf16 KV cache (block 256) and fp32 GDN states.
-    Heads are tensor-parallel over the ranks with an NCCL all-reduce after every output
-    projection; KV heads are replicated past TP 2."""
+    Heads are tensor-parallel over the ranks with an all-reduce after every output
+    projection (the one-shot NVLink kernel by default, NCCL with --allreduce nccl); KV heads
+    are replicated past TP 2."""
     from myvllm_b200 import workloads as W
     from myvllm_b200.cache.linear_attention_cache import LinearAttentionCache, PagedKVCache
     from myvllm_b200.layers.full_attention import GatedAttention
@@ -489,6 +490,13 @@ def run_c4(args, rank, world, device):
 
     torch.manual_seed(1234)  # identical weights on every rank (each loads its shard)
     S, hidden, n_layers, bs = 128, 2048, 48, 256
+    oneshot = None
+    if world > 1 and args.allreduce == "oneshot":
+        from myvllm_b200.layers import comm
+
+        # the o_proj / out_proj partial sums ([128, 2048] bf16, 512 KiB) go through the
+        # one-shot NVLink kernel instead of NCCL
+        oneshot = comm.enable_oneshot(max_bytes=2 << 20)
     kinds = ["full" if (i + 1) % 4 == 0 else "gdn" for i in range(n_layers)]
     layers = []
     for kind in kinds:
@@ -604,6 +612,8 @@ def run_c4(args, rank, world, device):
         t = torch.tensor([ms, e2e_ms], device=device, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, e2e_ms = t[0].item(), t[1].item()
+    if oneshot is not None:
+        comm.disable_oneshot()
     if rank != 0:
         return None
     hkv_rank = fa[0].num_kv_heads
@@ -618,6 +628,8 @@ def run_c4(args, rank, world, device):
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "c4: 36 GDN + 12 gated-attention layers, hidden 2048, 128 seqs, ctx ~U[1024,32768]",
                        "parallelism": f"tp{world}", "l2": "KV and states far larger than L2",
+                       "all_reduce": ("none" if world == 1 else
+                                      "one-shot NVLink kernel (mvb_allreduce_oneshot)" if oneshot is not None else "NCCL"),
                        "execution": "one CUDA graph per decode step"},
             "roofline": {"bound": "hbm", "kernel": "whole decode step (per rank)", "achieved": gbs,
                          "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": src,
@@ -660,6 +672,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3", "c4"])
+    ap.add_argument("--allreduce", default="oneshot", choices=["oneshot", "nccl"],
+                    help="c4 at N > 1: the tensor-parallel all-reduce after each output projection")
     ap.add_argument("--lengths", default=None,
                     help="c1/c3: sequence lengths instead of the config's seeded draw, e.g. 8x2048 or 700,1500 "
                          "(smaller cases for profiler captures)")

@@ -5,7 +5,8 @@
  * descriptors (device pointer + dtype + shape + strides in elements), enqueues its
  * kernels on the given CUDA stream (`void*` = cudaStream_t, NULL = legacy default
  * stream) and returns a status code.  Nothing here allocates device memory or
- * synchronises the host; callers own every buffer (outputs, states, workspaces).
+ * synchronises the host, except mvb_ipc_alloc, whose job is to allocate the shareable
+ * all-reduce buffer; callers own every buffer (outputs, states, workspaces).
  *
  * Reference interfaces replaced (paths relative to the reference project, `m/` =
  * `src/myvllm/`):
@@ -21,6 +22,8 @@
  *                                slot_mapping convention from m/utils/context.py:15)
  *   mvb_rmsnorm_gated           m/layers/norm.py:44-58                RMSNormGated.forward
  *   mvb_rmsnorm                 m/layers/norm.py:6-41                 RMSNorm.forward
+ *   mvb_allreduce_oneshot       m/layers/linear.py:159-164            the dist.all_reduce of
+ *                                                                     RowParallelLinear.forward
  *
  * Conventions kept from the reference:
  *   - index tensors (cu_seqlens, *_indices, block_tables, context_lens, slot_mapping) are int32;
@@ -182,6 +185,35 @@ int mvb_rmsnorm(const mvb_tensor* x, mvb_tensor* residual, const mvb_tensor* wei
  * tensor-core completion barrier gave up (the kernel abandoned its work and freed its
  * tensor memory).  Synchronises with the device. */
 int mvb_device_status(int* status);
+
+/* ---- tensor-parallel all-reduce over NVLink peer memory ----
+ * One buffer per rank, shared through CUDA IPC: each rank calls mvb_ipc_alloc, sends the
+ * 64-byte handle to the others (any host channel), and maps theirs with mvb_ipc_open.
+ * mvb_allreduce_oneshot then sums a bf16/f16 tensor over the ranks: every rank launches it
+ * on the same sequence of sizes, in the same order (the buffers carry per-block call
+ * counters, so a launch can be captured in a CUDA graph).  Waits for peers are bounded: one
+ * that gives up sets the device error word (mvb_device_status) and leaves that part of out
+ * unwritten.  No multicast: peer data moves by plain loads. */
+#define MVB_AR_MAX_RANKS 8
+typedef struct mvb_allreduce_peers {
+  int32_t world;                     /* ranks taking part, 2..MVB_AR_MAX_RANKS */
+  int32_t rank;                      /* this rank */
+  void* bufs[MVB_AR_MAX_RANKS];      /* every rank's buffer as mapped in this process (bufs[rank]: own) */
+  size_t buf_bytes;                  /* size of each buffer */
+} mvb_allreduce_peers;
+
+/* Buffer size for messages of up to max_message_bytes. */
+size_t mvb_allreduce_buffer_bytes(size_t max_message_bytes);
+/* cudaMalloc'd, zeroed buffer of `bytes` and its IPC handle (64 bytes written to `handle`). */
+int mvb_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+int mvb_ipc_free(void* dev_ptr);
+/* Maps another process's buffer from its 64-byte handle; mvb_ipc_close unmaps it. */
+int mvb_ipc_open(const void* handle, void** dev_ptr);
+int mvb_ipc_close(void* dev_ptr);
+/* out = sum over ranks of inp (contiguous, same shape and dtype; bytes a multiple of 16 and
+ * at most the buffer's slot size).  out may not alias inp. */
+int mvb_allreduce_oneshot(const mvb_allreduce_peers* peers, const mvb_tensor* inp, mvb_tensor* out,
+                          void* stream);
 
 /* Tensor-core self-test: D[128, n] = A B1 + (negate ? -1 : 1) A B2 on one CTA with
  * fp16 operands staged in the 128-byte-swizzle K-major (a_mn/b_mn = 0) or MN-major (= 1)

@@ -18,6 +18,7 @@ LIB_PATH = os.environ.get("MYVLLM_B200_LIB", os.path.join(_HERE, "_lib", "libmyv
 
 MAX_DIMS = 6
 MVB_F32, MVB_BF16, MVB_F16, MVB_I32 = 0, 1, 2, 3
+MVB_OK, MVB_ERR_ARG, MVB_ERR_UNSUPPORTED, MVB_ERR_CUDA = 0, 1, 2, 3
 _DTYPES = {torch.float32: MVB_F32, torch.bfloat16: MVB_BF16, torch.float16: MVB_F16, torch.int32: MVB_I32}
 _STATUS = {1: "bad argument", 2: "unsupported", 3: "CUDA error"}
 
@@ -29,6 +30,20 @@ class MvbTensor(ctypes.Structure):
         ("ndim", ctypes.c_int32),
         ("shape", ctypes.c_int64 * MAX_DIMS),
         ("stride", ctypes.c_int64 * MAX_DIMS),
+    ]
+
+
+AR_MAX_RANKS = 8
+
+
+class MvbAllReducePeers(ctypes.Structure):
+    """Mirror of ``mvb_allreduce_peers`` (include/myvllm_b200.h)."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("bufs", ctypes.c_void_p * AR_MAX_RANKS),
+        ("buf_bytes", ctypes.c_size_t),
     ]
 
 
@@ -59,6 +74,12 @@ SIGNATURES = {
     "mvb_rmsnorm_gated": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, _T, _P]),
     "mvb_rmsnorm": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, ctypes.c_int, _T, _P]),
     "mvb_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "mvb_allreduce_buffer_bytes": (ctypes.c_size_t, [ctypes.c_size_t]),
+    "mvb_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
+    "mvb_ipc_free": (ctypes.c_int, [_P]),
+    "mvb_ipc_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "mvb_ipc_close": (ctypes.c_int, [_P]),
+    "mvb_allreduce_oneshot": (ctypes.c_int, [ctypes.POINTER(MvbAllReducePeers), _T, _T, _P]),
     "mvb_selftest_umma": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          ctypes.c_int, _P]),
 }

@@ -9,6 +9,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 
 #include "../../include/myvllm_b200.h"
 

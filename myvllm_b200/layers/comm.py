@@ -1,0 +1,105 @@
+"""The tensor-parallel all-reduce of the row-parallel output projections.
+
+The reference sums the partial outputs of ``RowParallelLinear`` with
+``dist.all_reduce`` (``m/layers/linear.py:159-164``).  ``all_reduce`` below does the
+same through NCCL unless a :class:`OneShotAllReduce` is enabled for the group: then
+messages that fit its buffer (decode-size activations) are summed by the library's
+one-shot kernel over NVLink peer memory (``mvb_allreduce_oneshot``), and larger ones
+still go to NCCL.  Every rank of the group must make the same sequence of calls.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from .. import _lib
+
+
+class OneShotAllReduce:
+    """Per-rank IPC buffer shared with the other ranks of ``group``; a collective to
+    construct (every rank of the group calls it) and to :meth:`close`."""
+
+    def __init__(self, group=None, max_bytes: int = 4 << 20):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if not 2 <= self.world <= _lib.AR_MAX_RANKS:
+            raise ValueError(f"OneShotAllReduce: {self.world} ranks (2..{_lib.AR_MAX_RANKS} supported)")
+        lib = _lib.load()
+        self.max_bytes = int(max_bytes)
+        self.buf_bytes = int(lib.mvb_allreduce_buffer_bytes(self.max_bytes))
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        _lib.check("OneShotAllReduce", lib.mvb_ipc_alloc(self.buf_bytes, ctypes.byref(ptr), handle))
+        self._own = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened = []
+        peers = _lib.MvbAllReducePeers()
+        peers.world, peers.rank, peers.buf_bytes = self.world, self.rank, self.buf_bytes
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                peers.bufs[r] = self._own
+                continue
+            p = ctypes.c_void_p()
+            _lib.check("OneShotAllReduce", lib.mvb_ipc_open(h, ctypes.byref(p)))
+            self._opened.append(p.value)
+            peers.bufs[r] = p.value
+        self.peers = peers
+        # every rank has mapped every buffer before any kernel may store into a peer's flags
+        dist.barrier(group=group)
+
+    def eligible(self, t: torch.Tensor) -> bool:
+        nbytes = t.numel() * t.element_size()
+        return (t.is_cuda and t.dtype in (torch.bfloat16, torch.float16) and t.is_contiguous()
+                and nbytes <= self.max_bytes and nbytes % 16 == 0 and t.data_ptr() % 16 == 0)
+
+    def __call__(self, t: torch.Tensor) -> torch.Tensor:
+        out = torch.empty_like(t)
+        _lib.call("allreduce_oneshot", "mvb_allreduce_oneshot", ctypes.byref(self.peers), _lib.desc(t),
+                  _lib.desc(out), _lib.stream_of(t))
+        return out
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's; collective (after the last use
+        on every rank)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        lib = _lib.load()
+        for p in self._opened:
+            lib.mvb_ipc_close(p)
+        dist.barrier(group=self.group)
+        lib.mvb_ipc_free(self._own)
+        self._own, self._opened = None, []
+
+
+_oneshot: dict = {}
+
+
+def enable_oneshot(group=None, max_bytes: int = 4 << 20) -> OneShotAllReduce:
+    """Collective: routes this group's eligible all-reduces through the one-shot kernel."""
+    ar = OneShotAllReduce(group, max_bytes)
+    _oneshot[group] = ar
+    return ar
+
+
+def disable_oneshot(group=None) -> None:
+    """Collective: back to NCCL for this group; frees the buffers."""
+    ar = _oneshot.pop(group, None)
+    if ar is not None:
+        ar.close()
+
+
+def all_reduce(t: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum of ``t`` over the ranks of ``group``; returns the result (``t`` itself when NCCL
+    reduces it in place)."""
+    ar = _oneshot.get(group)
+    if ar is not None and ar.eligible(t):
+        return ar(t)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    return t

@@ -18,6 +18,8 @@ import torch.distributed as dist
 import torch.nn.functional as F
 from torch import nn
 
+from . import comm
+
 
 def tp_rank_size(group=None) -> tuple[int, int]:
     if dist.is_available() and dist.is_initialized():
@@ -150,7 +152,7 @@ class RowParallelLinear(Linear):
         bias = self.bias if (self.bias is None or self.tp_rank == 0) else None
         result = F.linear(x, self.weight, bias)
         if self.tp_size > 1:
-            dist.all_reduce(result, op=dist.ReduceOp.SUM)
+            result = comm.all_reduce(result)
         return result
 
     def weight_loader(self, param: nn.Parameter, loaded_weights: torch.Tensor):

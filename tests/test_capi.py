@@ -33,6 +33,28 @@ def test_library_exports_every_declared_symbol():
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
 
 
+def test_allreduce_rejects_bad_arguments():
+    """The one-shot all-reduce validates its peers and tensors before touching a device."""
+    lib = _lib.load()
+    assert lib.mvb_allreduce_buffer_bytes(1 << 20) == 8192 + 2 * (1 << 20)
+    x = _fake([128, 2048])
+    y = _fake([128, 2048], ptr=0x200000)
+    peers = _lib.MvbAllReducePeers()
+    peers.world, peers.rank, peers.buf_bytes = 1, 0, lib.mvb_allreduce_buffer_bytes(1 << 20)
+    peers.bufs[0] = 0x10000
+    call = lambda: lib.mvb_allreduce_oneshot(ctypes.byref(peers), ctypes.byref(x), ctypes.byref(y), None)  # noqa: E731
+    assert call() == _lib.MVB_ERR_ARG  # one rank
+    peers.world = 2
+    assert call() == _lib.MVB_ERR_ARG  # rank 1's buffer is NULL
+    peers.bufs[1] = 0x20000
+    peers.buf_bytes = lib.mvb_allreduce_buffer_bytes(4096)
+    assert call() == _lib.MVB_ERR_ARG  # 512 KiB message, 4 KiB slots
+    peers.buf_bytes = lib.mvb_allreduce_buffer_bytes(1 << 20)
+    z = _fake([128, 2048], dtype=_lib.MVB_F32, ptr=0x200000)
+    assert lib.mvb_allreduce_oneshot(ctypes.byref(peers), ctypes.byref(z), ctypes.byref(z), None) == \
+        _lib.MVB_ERR_UNSUPPORTED  # fp32
+
+
 def test_version_and_error_string():
     lib = _lib.load()
     assert lib.mvb_version() >= 100
