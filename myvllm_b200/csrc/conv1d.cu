@@ -305,22 +305,33 @@ __global__ void __launch_bounds__(128) conv1d_update_kernel(ConvParams p) {
     if (j < W - 1) load_vec<T, TW, VEC>(st + j * p.ss_t, p.ss_c, xp[j]);
   float cur[VEC];
   load_vec<T, TW, VEC>(x, p.sx_c, cur);
+  // weights: the thread's VEC x W taps as 16-byte vectors when [dim, W] is contiguous (one
+  // scalar load per tap otherwise)
+  float w[W][VEC];
+  const TW* wt = wp + (int64_t)c0 * p.sw_c;
+  constexpr int kWv = 16 / sizeof(TW);
+  if (VEC == 8 && p.sw_j == 1 && p.sw_c == W && (VEC * W) % kWv == 0 && (reinterpret_cast<uintptr_t>(wt) & 15) == 0) {
+    TW wl[VEC * W];
+#pragma unroll
+    for (int v = 0; v < VEC * W / kWv; ++v) reinterpret_cast<uint4*>(wl)[v] = reinterpret_cast<const uint4*>(wt)[v];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i)
+#pragma unroll
+      for (int j = 0; j < W; ++j) w[j][i] = to_f32<TW>(wl[i * W + j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < W; ++j)
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) w[j][i] = to_f32<TW>(wt[(int64_t)i * p.sw_c + j * p.sw_j]);
+  }
   float acc[VEC];
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
+  for (int i = 0; i < VEC; ++i) {
+    float a = 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxW; ++j) {
-    if (j < W) {
-      float wj[VEC];
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) wj[i] = to_f32<TW>(wp[(int64_t)(c0 + i) * p.sw_c + j * p.sw_j]);
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) acc[i] += wj[i] * (j == W - 1 ? cur[i] : xp[j][i]);
-    }
+    for (int j = 0; j < W; ++j) a += w[j][i] * (j == W - 1 ? cur[i] : xp[j][i]);
+    acc[i] = p.silu ? __fdividef(a, 1.f + __expf(-a)) : a;
   }
-  if (p.silu)
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] = silu(acc[i]);
   store_vec<T, VEC>(out, p.so_c, acc);
 #pragma unroll
   for (int j = 0; j < kMaxW - 1; ++j) {
