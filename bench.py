@@ -489,7 +489,7 @@ def run_c4(args, rank, world, device):
     from myvllm_b200.utils.context import set_context
 
     torch.manual_seed(1234)  # identical weights on every rank (each loads its shard)
-    S, hidden, n_layers, bs = 128, 2048, 48, 256
+    S, hidden, n_layers, bs = args.seqs or 128, 2048, args.layers or 48, 256
     oneshot = None
     if world > 1 and args.allreduce == "oneshot":
         from myvllm_b200.layers import comm
@@ -626,7 +626,8 @@ def run_c4(args, rank, world, device):
     return {"metric": "decode us/step (48-layer hybrid stack, 128 seqs)", "value": ms * 1e3, "unit": "us",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "c4: 36 GDN + 12 gated-attention layers, hidden 2048, 128 seqs, ctx ~U[1024,32768]",
+            "config": {"workload": f"c4: {n_layers - n_layers // 4} GDN + {n_layers // 4} gated-attention layers, hidden 2048, "
+                                   f"{S} seqs, ctx ~U[1024,32768]",
                        "parallelism": f"tp{world}", "l2": "KV and states far larger than L2",
                        "all_reduce": ("none" if world == 1 else
                                       "one-shot NVLink kernel (mvb_allreduce_oneshot)" if oneshot is not None else "NCCL"),
@@ -672,6 +673,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3", "c4"])
+    ap.add_argument("--layers", type=int, default=None,
+                    help="c4: layers instead of 48 (a multiple of 4; smaller cases for profiler captures)")
+    ap.add_argument("--seqs", type=int, default=None, help="c4: sequences instead of 128 (profiler cases)")
     ap.add_argument("--allreduce", default="oneshot", choices=["oneshot", "nccl"],
                     help="c4 at N > 1: the tensor-parallel all-reduce after each output projection")
     ap.add_argument("--lengths", default=None,
