@@ -22,6 +22,7 @@
  *                                slot_mapping convention from m/utils/context.py:15)
  *   mvb_rmsnorm_gated           m/layers/norm.py:44-58                RMSNormGated.forward
  *   mvb_rmsnorm                 m/layers/norm.py:6-41                 RMSNorm.forward
+ *   mvb_rmsnorm_rope            m/layers/full_attention.py:49-64      q_norm/k_norm + rotary
  *   mvb_allreduce_oneshot       m/layers/linear.py:159-164            the dist.all_reduce of
  *                                                                     RowParallelLinear.forward
  *
@@ -178,6 +179,16 @@ int mvb_rmsnorm_gated(const mvb_tensor* x, const mvb_tensor* gate, const mvb_ten
  * Replaces RMSNorm.forward (m/layers/norm.py:6-41). */
 int mvb_rmsnorm(const mvb_tensor* x, mvb_tensor* residual, const mvb_tensor* weight, float eps,
                 int zero_centered_gamma, mvb_tensor* out, void* stream);
+
+/* The q/k norm and partial rotary of full attention in one pass (the layer's
+ * q_norm / k_norm, m/layers/full_attention.py:49-64, then apply_rotary_pos_emb on the first
+ * rotary_dim dims, m/layers/rotary_embedding.py:6-31): x, out [T, H, D] (D <= 256; head
+ * rows 16-byte aligned); weight [D] as mvb_rmsnorm; cos, sin [T, rotary_dim / 2] fp32 with
+ * rotary_dim a power of two in [16, D].  Half-split rotation: for c < rotary_dim / 2,
+ * (y_c, y_{c+r/2}) -> (y_c cos_c - y_{c+r/2} sin_c, y_{c+r/2} cos_c + y_c sin_c); fp32
+ * math, one rounding. */
+int mvb_rmsnorm_rope(const mvb_tensor* x, const mvb_tensor* weight, float eps, int zero_centered_gamma,
+                     const mvb_tensor* cos, const mvb_tensor* sin, mvb_tensor* out, void* stream);
 
 /* Diagnostics. */
 

@@ -73,6 +73,7 @@ SIGNATURES = {
     "mvb_store_kvcache": (ctypes.c_int, [_T, _T, _T, _T, _T, _P]),
     "mvb_rmsnorm_gated": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, _T, _P]),
     "mvb_rmsnorm": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, ctypes.c_int, _T, _P]),
+    "mvb_rmsnorm_rope": (ctypes.c_int, [_T, _T, ctypes.c_float, ctypes.c_int, _T, _T, _T, _P]),
     "mvb_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "mvb_allreduce_buffer_bytes": (ctypes.c_size_t, [ctypes.c_size_t]),
     "mvb_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),

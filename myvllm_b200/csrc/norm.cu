@@ -141,8 +141,107 @@ void launch_plain(const mvb_tensor* x, mvb_tensor* res, const mvb_tensor* w, mvb
 #undef MVB_NORM_CASE
 }
 
+// RMSNorm of each [D] row (D <= 256: one 16-byte vector per lane), then the half-split
+// rotary on its first rd dims: for c < rd/2, (y_c, y_{c+rd/2}) <- (y_c cos_c - y_{c+rd/2} sin_c,
+// y_{c+rd/2} cos_c + y_c sin_c), cos/sin [T, rd/2] fp32 at the row's token.  The partner of
+// lane l's dims is lane l ^ (rd/16) (rd/16 a power of two).  fp32 throughout, one rounding.
+template <typename T, typename TW>
+__global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const T* x, Rows3 rx, const TW* w, T* out, Rows3 ro,
+                                                           const float* cosp, const float* sinp, int64_t scs,
+                                                           int64_t sss, int64_t rows, int heads, int d, int rd,
+                                                           float eps, float w_offset) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;  // whole warps leave together (a warp is one row)
+  const int c = lane * 8;
+  const bool live = c < d;
+  float y[8];
+  float ss = 0.f;
+  if (live) {
+    unpack8<T>(*reinterpret_cast<const uint4*>(x + rx.at(row, heads) + c), y);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += y[j] * y[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = 0.f;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)d + eps);
+  if (live) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] *= r * (to_f32<TW>(w[c + j]) + w_offset);
+  }
+  const int half = rd >> 1;
+  float partner[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, y[j], half >> 3);
+  if (live && c < rd) {
+    const int64_t t = row / heads;
+    const int ci = c < half ? c : c - half;
+    const float sgn = c < half ? -1.f : 1.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float cs = cosp[t * scs + ci + j], sn = sinp[t * sss + ci + j];
+      y[j] = fmaf(sgn * partner[j], sn, y[j] * cs);
+    }
+  }
+  if (live) *reinterpret_cast<uint4*>(out + ro.at(row, heads) + c) = pack8<T>(y);
+}
+
+template <typename T, typename TW>
+void launch_rope(const mvb_tensor* x, const mvb_tensor* w, mvb_tensor* o, const mvb_tensor* cs, const mvb_tensor* sn,
+                 float eps, float w_off, cudaStream_t st) {
+  const int heads = (int)x->shape[1];
+  const int64_t rows = x->shape[0] * heads;
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  rmsnorm_rope_kernel<T, TW><<<blocks, 256, 0, st>>>(
+      static_cast<const T*>(x->data), rows3(x), static_cast<const TW*>(w->data), static_cast<T*>(o->data), rows3(o),
+      static_cast<const float*>(cs->data), static_cast<const float*>(sn->data), cs->stride[0], sn->stride[0], rows,
+      heads, (int)x->shape[2], (int)(2 * cs->shape[1]), eps, w_off);
+}
+
 }  // namespace
 }  // namespace mvb
+
+extern "C" int mvb_rmsnorm_rope(const mvb_tensor* x, const mvb_tensor* weight, float eps, int zero_centered_gamma,
+                                const mvb_tensor* cos, const mvb_tensor* sin, mvb_tensor* out, void* stream) {
+  using namespace mvb;
+  const char* op = "rmsnorm_rope";
+  int rc;
+  if ((rc = check_tensor(x, op, "x", 3)) || (rc = check_tensor(weight, op, "weight", 1)) ||
+      (rc = check_tensor(cos, op, "cos", 2)) || (rc = check_tensor(sin, op, "sin", 2)) ||
+      (rc = check_tensor(out, op, "out", 3)))
+    return rc;
+  for (int i = 0; i < 3; ++i) MVB_CHECK_ARG(out->shape[i] == x->shape[i], "%s: x/out shapes differ", op);
+  const int64_t d = x->shape[2], rd = 2 * cos->shape[1];
+  MVB_CHECK_ARG(weight->shape[0] == d, "%s: weight must be [D]", op);
+  MVB_CHECK_ARG(cos->shape[0] >= x->shape[0] && sin->shape[0] >= x->shape[0] && sin->shape[1] == cos->shape[1],
+                "%s: cos/sin must be [T, rotary_dim / 2]", op);
+  MVB_CHECK_ARG(x->dtype == out->dtype && (x->dtype == MVB_BF16 || x->dtype == MVB_F16),
+                "%s: x/out must share a 16-bit float dtype", op);
+  MVB_CHECK_ARG(weight->dtype == MVB_F32 || weight->dtype == x->dtype, "%s: weight dtype", op);
+  MVB_CHECK_ARG(cos->dtype == MVB_F32 && sin->dtype == MVB_F32, "%s: cos/sin must be fp32", op);
+  bool rows_ok = weight->stride[0] == 1 && cos->stride[1] == 1 && sin->stride[1] == 1;
+  for (const mvb_tensor* t : {x, static_cast<const mvb_tensor*>(out)})
+    rows_ok = rows_ok && t->stride[2] == 1 && t->stride[0] % 8 == 0 && t->stride[1] % 8 == 0 && aligned16(t->data);
+  const bool pow2 = rd >= 16 && (rd & (rd - 1)) == 0;
+  MVB_CHECK_SUPPORTED(d % 8 == 0 && d <= 256 && pow2 && rd <= d && rows_ok,
+                      "%s: needs D %% 8 == 0, D <= 256, rotary dims a power of two in [16, D], "
+                      "contiguous 16-byte aligned rows", op);
+  if (x->shape[0] * x->shape[1] == 0) return MVB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float w_off = zero_centered_gamma ? 1.f : 0.f;
+  const bool w32 = weight->dtype == MVB_F32;
+  if (x->dtype == MVB_BF16) {
+    if (w32) launch_rope<__nv_bfloat16, float>(x, weight, out, cos, sin, eps, w_off, st);
+    else launch_rope<__nv_bfloat16, __nv_bfloat16>(x, weight, out, cos, sin, eps, w_off, st);
+  } else {
+    if (w32) launch_rope<__half, float>(x, weight, out, cos, sin, eps, w_off, st);
+    else launch_rope<__half, __half>(x, weight, out, cos, sin, eps, w_off, st);
+  }
+  MVB_CHECK_LAUNCH(op);
+  return MVB_OK;
+}
 
 extern "C" int mvb_rmsnorm_gated(const mvb_tensor* x, const mvb_tensor* gate, const mvb_tensor* weight, float eps,
                                  mvb_tensor* out, void* stream) {

@@ -78,12 +78,14 @@ class GatedAttention(nn.Module):
         else:
             qg, kp, vp = self.q_proj(x), self.k_proj(x), self.v_proj(x)
         q, gate = torch.chunk(qg.view(T, self.num_q_heads, 2 * D), 2, dim=-1)
-        q = self.q_norm(q)
-        k = self.k_norm(kp.view(T, self.num_kv_heads, D))
         v = vp.view(T, self.num_kv_heads, Dv)
         if rotary_pos_emb_cos is not None and rotary_pos_emb_sin is not None:
-            q = apply_partial_rotary(q, rotary_pos_emb_cos, rotary_pos_emb_sin)
-            k = apply_partial_rotary(k, rotary_pos_emb_cos, rotary_pos_emb_sin)
+            # q/k norm and partial rotary in one kernel per tensor
+            q = self.q_norm.rope_forward(q, rotary_pos_emb_cos, rotary_pos_emb_sin)
+            k = self.k_norm.rope_forward(kp.view(T, self.num_kv_heads, D), rotary_pos_emb_cos, rotary_pos_emb_sin)
+        else:
+            q = self.q_norm(q)
+            k = self.k_norm(kp.view(T, self.num_kv_heads, D))
         cached = self.k_cache.numel() > 0
         if cached and ctx.slot_mapping is not None:
             store_kvcache(k, v, self.k_cache, self.v_cache, ctx.slot_mapping)

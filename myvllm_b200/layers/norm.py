@@ -61,6 +61,23 @@ class RMSNorm(nn.Module):
         y = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps) * weight
         return y.to(x.dtype)
 
+    def rope_forward(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """``apply_partial_rotary(rms(x), cos, sin)`` for x [T, H, D] -- the q/k norm and
+        rotary of full attention -- in one kernel (``mvb_rmsnorm_rope``) on CUDA 16-bit
+        tensors; the two reference steps otherwise."""
+        rd = 2 * cos.shape[-1]
+        if x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and x.dim() == 3 and x.stride(-1) == 1 and \
+                x.shape[-1] % 8 == 0 and x.shape[-1] <= 256 and 16 <= rd <= x.shape[-1] and (rd & (rd - 1)) == 0:
+            out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+            c32, s32 = cos.to(torch.float32).contiguous(), sin.to(torch.float32).contiguous()
+            _lib.call("RMSNorm.rope", "mvb_rmsnorm_rope", _lib.desc(x), _lib.desc(self.weight.detach()),
+                      float(self.eps), int(self.zero_centered_gamma), _lib.desc(c32), _lib.desc(s32), _lib.desc(out),
+                      _lib.stream_of(x))
+            return out
+        from .rotary_embedding import apply_partial_rotary
+
+        return apply_partial_rotary(self.rms_forward(x), cos, sin)
+
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None):
         """``rms(x)``; with ``residual``: ``(rms(x + residual), x + residual)``, the sum also
         written into ``residual`` (the fused pre-norm of a decoder step).  The reference

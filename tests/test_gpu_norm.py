@@ -75,3 +75,26 @@ def test_norms_on_two_stride_head_views():
     ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * gated.weight.float() * \
         torch.nn.functional.silu(z.float())
     assert_close(gated(x, z), ref)
+
+
+@pytest.mark.parametrize("d,rd,heads", [(256, 64, 16), (128, 128, 4), (256, 16, 2)])
+def test_rmsnorm_rope_matches_norm_then_rotary(d, rd, heads):
+    """Fused q/k norm + partial rotary (mvb_rmsnorm_rope) against the layer's two steps in
+    fp32 (m/layers/full_attention.py:49-64, m/layers/rotary_embedding.py:6-31), on a strided
+    head view like the fused projection's q."""
+    from myvllm_b200.layers.norm import RMSNorm
+    from myvllm_b200.layers.rotary_embedding import RotaryEmbedding, apply_partial_rotary
+
+    g = torch.Generator().manual_seed(d + rd)
+    T = 37
+    norm = RMSNorm((d,), 1e-6, True).cuda()
+    norm.weight.data = (0.1 * torch.randn(d, generator=g)).cuda()
+    base = torch.randn(T, heads, 2 * d, generator=g).to(torch.bfloat16).cuda()
+    x = base[:, :, :d]  # strided rows, as q out of the fused q|gate projection
+    pos = torch.randint(0, 30000, (T,), generator=g).cuda()
+    cos, sin = RotaryEmbedding(rd, 10_000_000.0).cuda().cos_sin(pos)
+    out = norm.rope_forward(x, cos, sin)
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * (norm.weight.float() + 1.0)
+    ref = apply_partial_rotary(y, cos.float(), sin.float())
+    assert_close(out, ref)
