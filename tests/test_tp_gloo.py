@@ -38,6 +38,8 @@ def _worker(rank, world, port, case, results):
             y = row(col(x))
             ref = (x @ w1.T + b1) @ w2.T + b2
             assert torch.allclose(y, ref, atol=1e-4), (y - ref).abs().max()
+        # shard GEMMs and full GEMMs may take different BLAS kernels: fp32 rounding-level
+        # differences (~1e-6) are expected, hence the absolute tolerances below
         elif case == "qkv":
             m = L.QKVParallelLinear(hidden, 4, 4, 8, 4, 4, 6)
             w = torch.randn(4 * 4 + 4 * 4 + 8 * 6, hidden)
@@ -46,16 +48,16 @@ def _worker(rank, world, port, case, results):
             q, k, v = full[:, :16], full[:, 16:32], full[:, 32:]
             mine = m(x)
             qs, ks, vs = 4 * 2, 4 * 2, 8 * 3
-            assert torch.allclose(mine[:, :qs], q[:, rank * qs:(rank + 1) * qs])
-            assert torch.allclose(mine[:, qs:qs + ks], k[:, rank * ks:(rank + 1) * ks])
-            assert torch.allclose(mine[:, qs + ks:], v[:, rank * vs:(rank + 1) * vs])
+            assert torch.allclose(mine[:, :qs], q[:, rank * qs:(rank + 1) * qs], atol=1e-5)
+            assert torch.allclose(mine[:, qs:qs + ks], k[:, rank * ks:(rank + 1) * ks], atol=1e-5)
+            assert torch.allclose(mine[:, qs + ks:], v[:, rank * vs:(rank + 1) * vs], atol=1e-5)
         elif case == "gated_q":
             m = L.GatedQParallelLinear(hidden, 8, 4)
             w = torch.randn(4 * 16, hidden)
             m.weight_loader(m.weight, w)
             full = (x @ w.T).view(5, 4, 16)
             mine = m(x).view(5, 2, 16)
-            assert torch.allclose(mine, full[:, rank * 2:(rank + 1) * 2])
+            assert torch.allclose(mine, full[:, rank * 2:(rank + 1) * 2], atol=1e-5)
         elif case == "kv_replicated":
             for heads in (2, 1):  # split at tp <= heads, replicated at tp > heads
                 m = L.KVParallelLinear(hidden, 8, heads)
@@ -64,7 +66,7 @@ def _worker(rank, world, port, case, results):
                 full = (x @ w.T).view(5, heads, 8)
                 head = rank if heads == 2 else 0
                 assert m.num_kv_heads == 1
-                assert torch.allclose(m(x).view(5, 8), full[:, head])
+                assert torch.allclose(m(x).view(5, 8), full[:, head], atol=1e-5)
         elif case == "layers":
             from myvllm_b200.layers.full_attention import GatedAttention
             from myvllm_b200.layers.linear_attention import GatedDeltaNet
