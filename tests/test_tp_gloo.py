@@ -78,6 +78,37 @@ def _worker(rank, world, port, case, results):
             att = GatedAttention(64, 16, 16, 16, 2, False, 1e-6)
             assert att.num_q_heads == 8 and att.num_kv_heads == 1
             assert att.o_proj.weight.shape == (64, 8 * 16)
+        elif case == "comm_dispatch":
+            # comm.all_reduce: the collective by default; an enabled one-shot object takes the
+            # tensors it calls eligible (a stand-in here: IPC buffers need GPUs)
+            from myvllm_b200.layers import comm
+
+            t = torch.full((4,), float(rank + 1))
+            assert comm.all_reduce(t) is t and torch.equal(t, torch.full((4,), 3.0))
+
+            class Fake:
+                calls = 0
+
+                def eligible(self, x):
+                    return x.numel() <= 4
+
+                def __call__(self, x):
+                    Fake.calls += 1
+                    return x * 10
+
+            comm._oneshot[None] = Fake()
+            try:
+                small = comm.all_reduce(torch.ones(4))
+                assert Fake.calls == 1 and torch.equal(small, torch.full((4,), 10.0))
+                big = torch.ones(8)
+                assert comm.all_reduce(big) is big and torch.equal(big, torch.full((8,), 2.0)) and Fake.calls == 1
+                # the row-parallel layer routes its partial sums through the same function
+                row = L.RowParallelLinear(8, 4)
+                row.weight.data.fill_(1.0)
+                y = row(torch.ones(1, 4))  # this rank's half of the 8 input features
+                assert Fake.calls == 2 and torch.equal(y, torch.full((1, 4), 40.0))
+            finally:
+                comm._oneshot.pop(None, None)
         results.put((rank, None))
     except Exception as e:  # report to the parent instead of hanging it
         results.put((rank, repr(e)))
@@ -86,7 +117,7 @@ def _worker(rank, world, port, case, results):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["column_row", "qkv", "gated_q", "kv_replicated", "layers"])
+@pytest.mark.parametrize("case", ["column_row", "qkv", "gated_q", "kv_replicated", "layers", "comm_dispatch"])
 def test_tp2_gloo(case):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
