@@ -6,7 +6,8 @@
 // ctx - L + i.
 //
 // One CTA = 128 query rows of one (sequence, q-head), 6 warps with fixed roles:
-//   warp 0     TMA producer: Q once, then K/V tiles of 64 keys into a 2- or 3-stage ring
+//   warp 0     TMA producer: Q once, then K/V tiles of BN keys (128 at D = 256, else 64)
+//              into a 1- or 3-stage ring
 //              (3-D maps [T, H, D] for contiguous K/V; 4-D maps [blocks, bs, H, D] for the
 //              paged cache, one box per page segment);
 //   warp 1     MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score buffers,
@@ -28,11 +29,17 @@ namespace {
 
 using namespace umma;
 
+// keys per K/V tile for head dim d
+constexpr int fa_tc_bn(int d) { return d == 256 ? 128 : 64; }
+
 template <int D>
 struct FaTc {
   static constexpr int BM = 128;
-  static constexpr int BN = 64;
-  static constexpr int NS = D == 256 ? 2 : 3;  // K/V ring stages
+  // D = 256 takes 128-key tiles (half as many, twice as wide score MMAs) with one K/V stage
+  // and one P buffer, which is what fits; the producer then issues K_{j+1} before V_j.
+  static constexpr int BN = fa_tc_bn(D);
+  static constexpr int NS = D == 256 ? 1 : 3;  // K/V ring stages
+  static constexpr int NP = D == 256 ? 1 : 2;  // P buffers
   static constexpr int DB = D / 64;
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KV_BYTES = BN * D * 2;
@@ -40,7 +47,7 @@ struct FaTc {
   static constexpr uint32_t OFF_K = Q_BYTES;
   static constexpr uint32_t OFF_V = OFF_K + NS * KV_BYTES;
   static constexpr uint32_t OFF_P = OFF_V + NS * KV_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_P + NP * P_BYTES;
   static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(D + 2 * BN <= 512, "TMEM budget");
@@ -81,7 +88,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t phase) {
 template <typename T, int D, bool PAGED>
 __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constant__ FaTcParams p) {
   using C = FaTc<D>;
-  constexpr int BM = C::BM, BN = C::BN, NS = C::NS, DB = C::DB;
+  constexpr int BM = C::BM, BN = C::BN, NS = C::NS, NP = C::NP, DB = C::DB;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = align1024(smem_raw);
@@ -151,16 +158,23 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       };
       int k_issued = 0, v_issued = 0;
       bool ok = true;
+      // K_j goes out before V_{j-1}: with one stage, V_{j-1} waits for PV_{j-2}, and the
+      // scores of tile j must not wait behind it
+      auto load_v = [&](int i) -> bool {
+        const int s = i % NS;
+        if (i >= NS && !mbar_wait(&bars->v_empty[s], ((i / NS) & 1) ^ 1)) return false;
+        load_tile(&p.tm_v, smem + C::OFF_V + s * C::KV_BYTES, i * BN, &bars->v_full[s]);
+        v_issued = i + 1;
+        return true;
+      };
       for (int j = 0; j < n_tiles; ++j) {
         const int s = j % NS;
-        const uint32_t ph = (uint32_t)((j / NS) & 1);
-        if (j >= NS && !(ok = mbar_wait(&bars->k_empty[s], ph ^ 1))) break;
+        if (j >= NS && !(ok = mbar_wait(&bars->k_empty[s], ((j / NS) & 1) ^ 1))) break;
         load_tile(&p.tm_k, smem + C::OFF_K + s * C::KV_BYTES, j * BN, &bars->k_full[s]);
         k_issued = j + 1;
-        if (j >= NS && !(ok = mbar_wait(&bars->v_empty[s], ph ^ 1))) break;
-        load_tile(&p.tm_v, smem + C::OFF_V + s * C::KV_BYTES, j * BN, &bars->v_full[s]);
-        v_issued = j + 1;
+        if (j >= 1 && !(ok = load_v(j - 1))) break;
       }
+      if (ok) ok = load_v(n_tiles - 1);
       if (!ok) report_device_error(kErrFa);
       // drain: the copies of the last tiles must have landed before the CTA exits
       mbar_wait(&bars->q_full, 0);
@@ -177,14 +191,14 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       auto issue_pv = [&](int i) -> bool {
         const int s = i % NS;
         if (!mbar_wait(&bars->v_full[s], (i / NS) & 1)) return false;
-        if (!mbar_wait(&bars->p_full[i & 1], (i >> 1) & 1)) return false;
+        if (!mbar_wait(&bars->p_full[i % NP], (i / NP) & 1)) return false;
         fence_after();
-        const uint32_t pa = smem_u32(smem + C::OFF_P + (i & 1) * C::P_BYTES);
+        const uint32_t pa = smem_u32(smem + C::OFF_P + (i % NP) * C::P_BYTES);
         const uint32_t va = smem_u32(smem + C::OFF_V + s * C::KV_BYTES);
 #pragma unroll
         for (int ks = 0; ks < BN / 16; ++ks)
           mma_f16(tmem, desc_kmajor(pa, BM, ks), desc_mnmajor(va, BN * 128, ks), id_o, i > 0 || ks > 0);
-        commit(&bars->p_free[i & 1]);
+        commit(&bars->p_free[i % NP]);
         commit(&bars->v_empty[s]);
         return true;
       };
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       const bool grow = m_new > m + 8.f;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // rescale this warp's output rows once PV_{j-1} has landed
-        if (!(ok = warp_wait(&bars->p_free[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;
+        if (!(ok = warp_wait(&bars->p_free[(j - 1) % NP], ((j - 1) / NP) & 1))) break;
         fence_after();
         const float f = grow ? ex2(m - m_new) : 1.f;
 #pragma unroll 1
@@ -263,8 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       }
       if (grow) m = m_new;
       const float nbase = m == -INFINITY ? 0.f : -m;
-      if (j >= 2 && !(ok = warp_wait(&bars->p_free[j & 1], ((j - 2) >> 1) & 1))) break;
-      char* pb = smem + C::OFF_P + (j & 1) * C::P_BYTES;
+      if (j >= NP && !(ok = warp_wait(&bars->p_free[j % NP], ((j - NP) / NP) & 1))) break;
+      char* pb = smem + C::OFF_P + (j % NP) * C::P_BYTES;
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c8 = 0; c8 < BN / 8; ++c8) {
@@ -281,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       fence_async_smem();
       fence_before();
       __syncwarp();
-      if (lane == 0) tma::arrive(&bars->p_full[j & 1]);
+      if (lane == 0) tma::arrive(&bars->p_full[j % NP]);
     }
     if (ok && n_tiles > 0) ok = warp_wait(&bars->o_done, 0);
     if (ok) {
@@ -393,7 +407,7 @@ int launch_fa_tc(const FaParams& p, int dtype, int d, bool paged, int64_t T_q, i
       !aligned_stride(p.sv_t) || !aligned_stride(p.sv_h) || !aligned_stride(p.so_t) || !aligned_stride(p.so_h))
     return -1;
   if (paged) {
-    const int bn = 64;  // FaTc<D>::BN
+    const int bn = fa_tc_bn(d);
     const int bs = p.block_size;
     // a K/V tile is one page segment (bs >= BN) or whole pages of >= 8 rows (bs < BN)
     const bool tiles_ok = bs >= bn ? bs % bn == 0 : (bn % bs == 0 && bs % 8 == 0);
