@@ -6,8 +6,8 @@
 // ctx - L + i.
 //
 // One CTA = 128 query rows of one (sequence, q-head), 6 warps with fixed roles:
-//   warp 0     TMA producer: Q once, then K/V tiles of BN keys (128 at D = 256, else 64)
-//              into a 1- or 3-stage ring
+//   warp 0     TMA producer: Q once, then K/V tiles of 128 keys into a 1-, 2- or 3-stage
+//              ring (by head dim 256, 128, 64), K_j issued ahead of V_{j-1}
 //              (3-D maps [T, H, D] for contiguous K/V; 4-D maps [blocks, bs, H, D] for the
 //              paged cache, one box per page segment);
 //   warp 1     MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score buffers,
@@ -29,16 +29,16 @@ namespace {
 
 using namespace umma;
 
-// keys per K/V tile for head dim d
-constexpr int fa_tc_bn(int d) { return d == 256 ? 128 : 64; }
+// keys per K/V tile: 128, so each score MMA is 128 x 128 (narrower tiles leave the tensor
+// pipe idle between short MMAs); the host's paged-layout check uses the same number
+constexpr int fa_tc_bn(int) { return 128; }
 
 template <int D>
 struct FaTc {
   static constexpr int BM = 128;
-  // D = 256 takes 128-key tiles (half as many, twice as wide score MMAs) with one K/V stage
-  // and one P buffer, which is what fits; the producer then issues K_{j+1} before V_j.
+  // what fits in 227 KB next to Q: at D = 256 one K/V stage and one P buffer
   static constexpr int BN = fa_tc_bn(D);
-  static constexpr int NS = D == 256 ? 1 : 3;  // K/V ring stages
+  static constexpr int NS = D == 256 ? 1 : D == 128 ? 2 : 3;  // K/V ring stages
   static constexpr int NP = D == 256 ? 1 : 2;  // P buffers
   static constexpr int DB = D / 64;
   static constexpr uint32_t Q_BYTES = BM * D * 2;
