@@ -480,6 +480,7 @@ def run_c4(args, rank, world, device):
     Heads are tensor-parallel over the ranks with an all-reduce after every output
     projection (the one-shot NVLink kernel by default, NCCL with --allreduce nccl); KV heads
     are replicated past TP 2."""
+    from myvllm_b200 import _lib
     from myvllm_b200 import workloads as W
     from myvllm_b200.cache.linear_attention_cache import LinearAttentionCache, PagedKVCache
     from myvllm_b200.layers.full_attention import GatedAttention
@@ -576,8 +577,10 @@ def run_c4(args, rank, world, device):
         torch.cuda.current_stream().wait_stream(side)
         graph = torch.cuda.CUDAGraph()
         load_meta(args.warmup)
+        calls0 = _lib.n_calls
         with torch.cuda.graph(graph):
             out_static = step_static()
+        calls_per_step = _lib.n_calls - calls0  # library entry points captured in one step
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
@@ -637,7 +640,10 @@ def run_c4(args, rank, world, device):
                          "bytes_per_step_rank0": step_bytes, "traffic": None},
             "e2e": {"value": e2e_ms * 1e3, "unit": "us", "h2d_bytes_per_step": xh.numel() * 2,
                     "d2h_bytes_per_step": oh.numel() * 2},
-            "gpu_launches": None, "clocks": clk.summary()}
+            "gpu_launches": calls_per_step * args.steps,
+            "gpu_launches_note": "library entry-point calls in the captured step x steps (each launches one or more "
+                                 "kernels; the GEMMs are cuBLAS)",
+            "clocks": clk.summary()}
 
 
 # ------------------------------------------------------------------------ reference ----

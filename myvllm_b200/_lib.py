@@ -147,8 +147,13 @@ def check(op: str, status: int) -> None:
         raise RuntimeError(f"{op}: {_STATUS.get(status, status)}: {msg}")
 
 
+n_calls = 0  # entry-point calls made through call(): each launches one or more kernels
+
+
 def call(op: str, fn_name: str, *args) -> None:
     """Calls an int-returning entry point and raises on a non-zero status."""
+    global n_calls
+    n_calls += 1
     lib = load()
     wrapped = [ctypes.byref(a) if isinstance(a, MvbTensor) else a for a in args]
     check(op, getattr(lib, fn_name)(*wrapped))
