@@ -174,11 +174,12 @@ def test_paged_prefill_with_prior_context_vs_oracle():
     assert_close(o, ref)
 
 
-@pytest.mark.parametrize("bs", [16, 48, 128, 256])
+@pytest.mark.parametrize("bs", [16, 48, 64, 128, 192, 256])
 @pytest.mark.parametrize("d", [64, 256])
 def test_paged_prefill_block_sizes_vs_oracle(bs, d):
-    """Block sizes below, inside and above the 64-key K/V tile (16: four pages per tile;
-    48: pages straddle tiles, served by the mma.sync kernel; 128/256: one page segment)."""
+    """Block sizes below, inside and above the 128-key K/V tile (16 / 64: eight / two pages
+    per tile; 128 / 256: one page segment per tile; 48 and 192: pages straddle tiles,
+    served by the mma.sync kernel)."""
     ctx = [700, 40, 129, 1]
     new = [300, 40, 64, 1]
     kc, vc, bt = _paged(ctx, 2, d, bs, seed=bs + d)
