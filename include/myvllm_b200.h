@@ -72,7 +72,7 @@ int mvb_version(void);
 /* Message for the last non-zero status returned on the calling host thread. */
 const char* mvb_last_error(void);
 
-/* Varlen causal depthwise conv (width W <= 8) + SiLU over packed sequences.
+/* Varlen causal depthwise conv (width 2 <= W <= 6) + SiLU over packed sequences.
  * x [T, dim]; weight [dim, W]; conv_state [S_max, W-1, dim] (read as history, then
  * overwritten with the last W-1 inputs of each sequence); conv_state_indices [S];
  * cu_seqlens [S+1]; out [T, dim] (same dtype as x).  activation: 1 = SiLU, 0 = none. */
@@ -148,8 +148,9 @@ int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor* k_cache, c
 /* Allocation-free variant of mvb_paged_attention_decode (no counterpart in the reference).
  * For callers that may not allocate device memory when they decode: the split-KV partial
  * results go to a fixed 16 MiB array in the library's device image instead of a caller
- * workspace.  It splits as far as that array allows and returns MVB_ERR_UNSUPPORTED when
- * n_seqs * num_kv_heads * (head_dim + 1) * 128 bytes (two splits) exceed 16 MiB.
+ * workspace.  A context is split only as far as that array holds the partials of every
+ * (sequence, kv head): n_splits * n_seqs * num_kv_heads * (head_v_dim + 1) * 64 bytes
+ * <= 16 MiB; when not even two splits fit, the decode runs unsplit, which needs no scratch.
  * The first call on each device looks up the array's device address (make it before any
  * stream capture).  All calls share the array: calls that overlap on the GPU race. */
 int mvb_paged_attention_decode_noalloc(const mvb_tensor* q, const mvb_tensor* k_cache, const mvb_tensor* v_cache,
@@ -202,9 +203,11 @@ int mvb_device_status(int* status);
  * 64-byte handle to the others (any host channel), and maps theirs with mvb_ipc_open.
  * mvb_allreduce_oneshot then sums a bf16/f16 tensor over the ranks: every rank launches it
  * on the same sequence of sizes, in the same order (the buffers carry per-block call
- * counters, so a launch can be captured in a CUDA graph).  Waits for peers are bounded: one
- * that gives up sets the device error word (mvb_device_status) and leaves that part of out
- * unwritten.  No multicast: peer data moves by plain loads. */
+ * counters, so a launch can be captured in a CUDA graph; every launch runs the same 64
+ * blocks, so calls of different sizes may follow each other with no host synchronisation).
+ * Waits for peers are bounded: one that gives up sets the device error word
+ * (mvb_device_status) and writes this rank's own input into that part of out instead of the
+ * sum.  No multicast: peer data moves by plain loads. */
 #define MVB_AR_MAX_RANKS 8
 typedef struct mvb_allreduce_peers {
   int32_t world;                     /* ranks taking part, 2..MVB_AR_MAX_RANKS */

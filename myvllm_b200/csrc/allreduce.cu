@@ -7,19 +7,26 @@
 //   [4096, 4352)   epochs  uint32 [64 blocks], this rank's per-block call counters
 //   [8192, ...)    data    2 slots x max_bytes
 //
-// A launch has nblk blocks; block b owns bytes [b chunk, (b+1) chunk) of the message and
-// synchronises only with block b of the other ranks:
+// Every launch runs all kBlocks (64) blocks, whatever the message size; block b owns bytes
+// [b chunk, (b+1) chunk) of the message (chunk = ceil(bytes / 64), rounded to 16 B; a block
+// whose range is empty still takes part) and synchronises only with block b of the other
+// ranks:
 //   1. copy this rank's chunk of the input into its own slot (e & 1), e = epoch + 1;
 //   2. store e into flags[slot][rank][b] of every peer (release, system scope), after the
 //      block's copy;
 //   3. wait (acquire, bounded) until every peer's flags[slot][peer][b] on this rank read e;
 //   4. read the chunk from every rank's slot, sum in fp32 in rank order (so every rank
 //      gets the same bits) and write the output chunk.
-// Two slots alternate: a rank reaches call e+2 only after it has seen every peer's flag of
-// call e+1, which the peers store only after their call e finished reading.  The counters
-// live in device memory, so a captured CUDA graph replays correctly.  Nothing here uses
-// multicast; peer data moves by plain loads.  A wait that gives up sets the device error
-// word and the block skips its sum.
+// Because every block runs on every call, the per-block call counters stay equal and all
+// blocks of a call use the same slot.  Two slots alternate: a rank starts call e+2 only
+// after its call e+1 finished, in which it saw a flag of call e+1 from every peer; a peer
+// stores those only after its own call e finished reading (kernels on one stream run in
+// order), so no peer still reads the slot that call e+2 overwrites, whatever the sizes of
+// the calls.  The counters live in device memory, so a captured CUDA graph replays
+// correctly.  Nothing here uses multicast; peer data moves by plain loads.  A wait that
+// gives up sets the device error word, and that block writes this rank's own input into
+// its part of out (a defined value, not the sum) so the caller can detect it through
+// mvb_device_status.
 #include "common.cuh"
 #include "tcgen05.cuh"  // report_device_error
 
@@ -27,7 +34,7 @@ namespace mvb {
 namespace {
 
 constexpr int kMaxRanks = MVB_AR_MAX_RANKS;
-constexpr int kMaxBlocks = 64;
+constexpr int kBlocks = 64;  // blocks of every launch (and flag slots per rank)
 constexpr int kThreads = 512;
 constexpr size_t kFlagsOff = 0, kEpochOff = 4096, kDataOff = 8192;
 constexpr uint32_t kSpinLimit = 1u << 22;  // polls with a short sleep each: about two seconds
@@ -64,7 +71,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(const __gri
   __syncthreads();
   const uint32_t e = s_epoch;
   const int slot = e & 1;
-  const size_t beg = (size_t)b * p.chunk;
+  const size_t beg = (size_t)b * p.chunk < p.nbytes ? (size_t)b * p.chunk : p.nbytes;
   const size_t end = beg + p.chunk < p.nbytes ? beg + p.chunk : p.nbytes;
   const char* in = static_cast<const char*>(p.inp);
   const size_t slot_off = kDataOff + (size_t)slot * p.max_bytes;
@@ -79,9 +86,9 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(const __gri
   const int peer = tid;
   if (peer < p.world && peer != p.rank) {
     __threadfence_system();
-    st_release_sys(reinterpret_cast<uint32_t*>(p.bufs[peer] + kFlagsOff) + (slot * kMaxRanks + p.rank) * kMaxBlocks + b,
+    st_release_sys(reinterpret_cast<uint32_t*>(p.bufs[peer] + kFlagsOff) + (slot * kMaxRanks + p.rank) * kBlocks + b,
                    e);
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(mine + kFlagsOff) + (slot * kMaxRanks + peer) * kMaxBlocks + b;
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(mine + kFlagsOff) + (slot * kMaxRanks + peer) * kBlocks + b;
     uint32_t it = 0;
     while (ld_acquire_sys(f) != e) {
       if (++it == kSpinLimit) {
@@ -94,20 +101,23 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(const __gri
   }
   __syncthreads();
 
-  // 4. the sum, in rank order
-  if (!s_fail) {
-    for (size_t i = beg + (size_t)tid * 16; i < end; i += (size_t)kThreads * 16) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int r = 0; r < p.world; ++r) {
-        const uint4 u = r == p.rank ? *reinterpret_cast<const uint4*>(in + i)
-                                    : __ldcg(reinterpret_cast<const uint4*>(p.bufs[r] + slot_off + i));
-        float f[8];
-        unpack8<T>(u, f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += f[j];
-      }
-      *reinterpret_cast<uint4*>(static_cast<char*>(p.out) + i) = pack8<T>(acc);
+  // 4. the sum, in rank order (after a failed wait: this rank's own input)
+  const bool failed = s_fail != 0;
+  for (size_t i = beg + (size_t)tid * 16; i < end; i += (size_t)kThreads * 16) {
+    const uint4 own = *reinterpret_cast<const uint4*>(in + i);
+    if (failed) {
+      *reinterpret_cast<uint4*>(static_cast<char*>(p.out) + i) = own;
+      continue;
     }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < p.world; ++r) {
+      const uint4 u = r == p.rank ? own : __ldcg(reinterpret_cast<const uint4*>(p.bufs[r] + slot_off + i));
+      float f[8];
+      unpack8<T>(u, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += f[j];
+    }
+    *reinterpret_cast<uint4*>(static_cast<char*>(p.out) + i) = pack8<T>(acc);
   }
   if (tid == 0) epochs[b] = e;
 }
@@ -197,15 +207,14 @@ extern "C" int mvb_allreduce_oneshot(const mvb_allreduce_peers* peers, const mvb
   p.nbytes = nbytes;
   p.world = peers->world;
   p.rank = peers->rank;
-  // 8 KB per block (512 threads x 16 B), at most 64 blocks
-  size_t nblk = (nbytes + 8191) / 8192;
-  if (nblk > (size_t)kMaxBlocks) nblk = kMaxBlocks;
-  p.chunk = ((nbytes + nblk - 1) / nblk + 15) / 16 * 16;
+  // always kBlocks blocks (see the header comment): the partition may change with the size,
+  // the slot each call uses may not
+  p.chunk = ((nbytes + kBlocks - 1) / kBlocks + 15) / 16 * 16;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (inp->dtype == MVB_BF16)
-    allreduce_oneshot_kernel<__nv_bfloat16><<<(unsigned)nblk, kThreads, 0, st>>>(p);
+    allreduce_oneshot_kernel<__nv_bfloat16><<<kBlocks, kThreads, 0, st>>>(p);
   else
-    allreduce_oneshot_kernel<__half><<<(unsigned)nblk, kThreads, 0, st>>>(p);
+    allreduce_oneshot_kernel<__half><<<kBlocks, kThreads, 0, st>>>(p);
   MVB_CHECK_LAUNCH(op);
   return MVB_OK;
 }

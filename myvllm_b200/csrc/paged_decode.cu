@@ -336,6 +336,7 @@ constexpr int kMaxSplits = 1024;
 
 // Chooses the split length (a multiple of the tile) for a context bound and batch.
 inline int decode_split_len(int64_t n_seqs, int64_t hkv, int64_t max_ctx, int64_t max_splits) {
+  if (max_splits <= 1) return (int)(((max_ctx + kTile - 1) / kTile) * kTile);  // one split: the whole context
   const int64_t per = n_seqs * hkv;
   // aim for >= 8 CTAs per SM of work (16 measured the same at config 4; 32 and more were
   // 45% slower)
@@ -473,9 +474,12 @@ extern "C" int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor*
 // latency-critical step where the allocator may synchronise the device.  This entry point
 // needs no workspace: the split-KV partial results go to a fixed array that is part of the
 // library's device image (every GPU that loads the library holds these 16 MiB until the
-// process exits).  Nothing in the array has to start at zero: each call writes every
-// partial it later reads.  All calls share the one array, so calls whose kernels overlap on
-// the GPU (e.g. on two streams) race; issue them in order.
+// process exits).  It splits a context only as far as the array holds the partials of
+// every (sequence, kv head); when not even two splits fit it runs unsplit, which needs no
+// scratch at all, exactly as the workspace entry point does without a workspace.  Nothing
+// in the array has to start at zero: each call writes every partial it later reads.  All
+// calls share the one array, so calls whose kernels overlap on the GPU (e.g. on two
+// streams) race; issue them in order.
 namespace mvb {
 namespace {
 
@@ -520,15 +524,10 @@ extern "C" int mvb_paged_attention_decode_noalloc(const mvb_tensor* q, const mvb
     return rc;
   const int64_t S = q->shape[0], hkv = k_cache->shape[2], dv = v_cache->shape[3];
   const size_t per_split = (size_t)(S > 0 ? S : 1) * (size_t)(hkv > 0 ? hkv : 1) * 16 * (size_t)(dv + 1) * sizeof(float);
-  const size_t fit = kDecodeScratchBytes / per_split;
-  if (fit < 2)
-    MVB_FAIL(MVB_ERR_UNSUPPORTED,
-             "%s: %lld sequences x %lld kv heads x head dim %lld need %zu bytes of split scratch for 2 splits; "
-             "the built-in scratch holds %zu bytes (use mvb_paged_attention_decode with a workspace)",
-             op, (long long)S, (long long)hkv, (long long)dv, 2 * per_split, kDecodeScratchBytes);
+  const size_t fit = kDecodeScratchBytes / per_split;  // splits whose partials fit the array
   void* scratch = nullptr;
   if ((rc = decode_scratch_address(&scratch))) return rc;
-  const int64_t max_splits = fit < (size_t)kMaxSplits ? (int64_t)fit : (int64_t)kMaxSplits;
+  const int64_t max_splits = fit < 1 ? 1 : (fit < (size_t)kMaxSplits ? (int64_t)fit : (int64_t)kMaxSplits);
   return run_paged_decode(op, q, k_cache, v_cache, block_tables, context_lens, scale, block_size, max_context_len, o,
                           scratch, kDecodeScratchBytes, max_splits, static_cast<cudaStream_t>(stream));
 }

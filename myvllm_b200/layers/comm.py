@@ -63,12 +63,23 @@ class OneShotAllReduce:
                   _lib.desc(out), _lib.stream_of(t))
         return out
 
+    def check(self) -> None:
+        """Raises if a one-shot launch since the last check gave up waiting for a peer.
+        Such a launch leaves this rank's own input (not the sum) in its output and sets the
+        library's device error word; reading the word synchronises the device, so call this
+        at a point that already waits (end of a step, before :meth:`close`)."""
+        status = _lib.device_status()
+        if status != 0:
+            raise RuntimeError(f"OneShotAllReduce: a peer did not answer within the wait limit "
+                               f"(device status {status}); outputs since the last check are partial sums")
+
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's; collective (after the last use
-        on every rank)."""
+        on every rank).  Raises, after releasing the buffers, if a launch gave up on a peer."""
         if self._own is None:
             return
         torch.cuda.synchronize()
+        status = _lib.device_status()
         dist.barrier(group=self.group)
         lib = _lib.load()
         for p in self._opened:
@@ -76,6 +87,9 @@ class OneShotAllReduce:
         dist.barrier(group=self.group)
         lib.mvb_ipc_free(self._own)
         self._own, self._opened = None, []
+        if status != 0:
+            raise RuntimeError(f"OneShotAllReduce: a peer did not answer within the wait limit "
+                               f"(device status {status}); some outputs were partial sums")
 
 
 _oneshot: dict = {}

@@ -31,7 +31,9 @@ import torch  # noqa: E402
 import torch.nn.functional as F  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.environ.get("REF_SRC", "/root/reference/src"))
+if not os.environ.get("REF_SRC"):
+    sys.exit("make_golden.py: set REF_SRC to the reference checkout's src/ directory")
+sys.path.insert(0, os.environ["REF_SRC"])
 
 
 def c0_inputs(seed: int = 0):

@@ -68,6 +68,22 @@ def _worker(rank, world, port, results):
                 peer = y.clone()
                 dist.broadcast(peer, 0)
                 assert torch.equal(y.view(torch.int16), peer.view(torch.int16)), (n, dtype)
+        # back-to-back calls of changing sizes with no host or collective synchronisation
+        # between them, while the ranks drift apart (a spin kernel on a different rank at each
+        # call): a slot overwritten while a lagging peer still reads it would mix two calls
+        sizes = [4096, 6144, 8, 131072, 4104, 262144, 16, 65536 + 8, 8, 128 * 2048, 4096, 6144]
+        ins, outs = [], []
+        for i, n in enumerate(sizes):
+            if i % world == rank:
+                torch.cuda._sleep(2_000_000)
+            x = torch.randn(n, generator=g, device=dev).to(torch.bfloat16)
+            ins.append(x)
+            outs.append(comm.all_reduce(x))
+        torch.cuda.synchronize()
+        for i, (x, y) in enumerate(zip(ins, outs)):
+            exact = exact_sum(x)
+            assert torch.equal(y.view(torch.int16), exact.view(torch.int16)), ("unsynchronised", i, sizes[i],
+                                                                               rel_err(y, exact))
         # too large for the buffer: NCCL takes it
         big = torch.ones(2 << 20, device=dev, dtype=torch.bfloat16)
         assert not ar.eligible(big), "a 4 MiB message must not fit the 2 MiB slots"

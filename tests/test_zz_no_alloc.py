@@ -59,11 +59,14 @@ def test_noalloc_decode_matches_workspace_entry_on_two_calls():
         assert_close(out, ref, what=f"noalloc decode (seed {kw['seed']})")
 
 
-def test_noalloc_decode_rejects_problems_beyond_its_scratch():
-    # 4096 sequences x 8 kv heads x 257 x 128 bytes is far beyond 16 MiB for two splits
-    q = torch.zeros(4096, 8, 256, dtype=torch.bfloat16, device="cuda")
-    kc = torch.zeros(1, 16, 8, 256, dtype=torch.bfloat16, device="cuda")
-    bt = torch.zeros(4096, 1, dtype=torch.int32, device="cuda")
-    ctx = torch.ones(4096, dtype=torch.int32, device="cuda")
-    with pytest.raises(RuntimeError, match="built-in scratch holds"):
-        _decode_noalloc(q, kc, kc, bt, ctx, 1 / 16, 16)
+def test_noalloc_decode_runs_unsplit_when_two_splits_do_not_fit():
+    # 256 sequences x 2 kv heads x head dim 256: the partials of two splits (2 x 8.4 MB) do
+    # not fit the 16 MiB array, so this entry point decodes every context in one split while
+    # the workspace entry point splits them (3 splits here); the results must still agree
+    rng = torch.Generator().manual_seed(5)
+    ctx = torch.randint(1, 3001, (256,), generator=rng).tolist()
+    q, kc, vc, bt, ctx_t = _problem(seed=5, ctx=ctx, hq=16, hkv=2, d=256, bs=256)
+    ref = paged_flash_attention_decode(q, kc, vc, bt, ctx_t, 1 / 16, 256)
+    out = _decode_noalloc(q, kc, vc, bt, ctx_t, 1 / 16, 256)
+    torch.cuda.synchronize()
+    assert_close(out, ref, what="noalloc decode, unsplit")
