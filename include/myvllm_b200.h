@@ -193,6 +193,24 @@ int mvb_rmsnorm_rope(const mvb_tensor* x, const mvb_tensor* weight, float eps, i
 
 /* Diagnostics. */
 
+/* Kernel family the last call of an op ran on the calling host thread.  Most ops have one
+ * path; these have a fallback for layouts their main kernel does not take:
+ *   MVB_OP_CHUNK_GDN      mvb_chunk_gated_delta_rule[_gated]: tensor-core (tcgen05) kernel,
+ *                         else the token-serial fp32 recurrence (same math, far slower);
+ *   MVB_OP_FA_PREFILL     mvb_flash_attention_prefill: tcgen05 + TMA kernel, else mma.sync;
+ *   MVB_OP_PAGED_PREFILL  mvb_paged_attention_prefill: tcgen05 + TMA kernel, else mma.sync.
+ * Returns MVB_PATH_* (MVB_PATH_NONE before the first call), or -1 for an unknown op.
+ * *reason (if reason != NULL) gets why the fallback was taken ("" on the main path); the
+ * string stays valid until the next call of that op on this thread. */
+#define MVB_OP_CHUNK_GDN 0
+#define MVB_OP_FA_PREFILL 1
+#define MVB_OP_PAGED_PREFILL 2
+#define MVB_PATH_NONE 0
+#define MVB_PATH_TENSOR_CORE 1  /* tcgen05.mma with TMEM accumulators, TMA-fed */
+#define MVB_PATH_SERIAL 2       /* token-serial recurrence on CUDA cores */
+#define MVB_PATH_MMA_SYNC 3     /* warp-level mma.sync kernel */
+int mvb_last_path(int op, const char** reason);
+
 /* Reads and clears the kernels' device error word: 0 = no error; 1 = a bounded wait on a
  * tensor-core completion barrier gave up (the kernel abandoned its work and freed its
  * tensor memory).  Synchronises with the device. */

@@ -75,6 +75,7 @@ SIGNATURES = {
     "mvb_rmsnorm": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, ctypes.c_int, _T, _P]),
     "mvb_rmsnorm_rope": (ctypes.c_int, [_T, _T, ctypes.c_float, ctypes.c_int, _T, _T, _T, _P]),
     "mvb_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "mvb_last_path": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p)]),
     "mvb_allreduce_buffer_bytes": (ctypes.c_size_t, [ctypes.c_size_t]),
     "mvb_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
     "mvb_ipc_free": (ctypes.c_int, [_P]),
@@ -149,6 +150,11 @@ def check(op: str, status: int) -> None:
 
 n_calls = 0  # entry-point calls made through call(): each launches one or more kernels
 
+# MYVLLM_B200_STRICT=1: after every entry point, wait for the device and raise if a kernel
+# reported a device-side failure (a bounded wait that gave up).  Debugging aid: it
+# synchronises after each op, so it is off by default and must stay off during graph capture.
+STRICT = os.environ.get("MYVLLM_B200_STRICT", "0") not in ("", "0")
+
 
 def call(op: str, fn_name: str, *args) -> None:
     """Calls an int-returning entry point and raises on a non-zero status."""
@@ -157,6 +163,26 @@ def call(op: str, fn_name: str, *args) -> None:
     lib = load()
     wrapped = [ctypes.byref(a) if isinstance(a, MvbTensor) else a for a in args]
     check(op, getattr(lib, fn_name)(*wrapped))
+    if STRICT:
+        status = device_status()
+        if status != 0:
+            raise RuntimeError(f"{op}: a kernel reported device status {status} (a bounded wait gave up; "
+                               "the output is not valid)")
+
+
+OP_CHUNK_GDN, OP_FA_PREFILL, OP_PAGED_PREFILL = 0, 1, 2
+PATHS = {0: "none", 1: "tensor_core", 2: "serial", 3: "mma_sync"}
+
+
+def last_path(op: int) -> tuple[str, str]:
+    """(kernel family, fallback reason) of the last call of ``op`` on this thread:
+    "tensor_core" is the tcgen05 kernel; "serial" / "mma_sync" are the fallbacks for layouts
+    it does not take, with the reason."""
+    reason = ctypes.c_char_p()
+    code = load().mvb_last_path(int(op), ctypes.byref(reason))
+    if code < 0:
+        raise ValueError(f"last_path: unknown op {op}")
+    return PATHS.get(code, str(code)), (reason.value or b"").decode(errors="replace")
 
 
 _workspaces: dict = {}

@@ -7,6 +7,16 @@ namespace mvb {
 
 static thread_local char g_last_error[512] = "";
 
+constexpr int kPathOps = 3;  // MVB_OP_CHUNK_GDN, MVB_OP_FA_PREFILL, MVB_OP_PAGED_PREFILL
+static thread_local int g_path[kPathOps] = {MVB_PATH_NONE, MVB_PATH_NONE, MVB_PATH_NONE};
+static thread_local char g_path_reason[kPathOps][160] = {"", "", ""};
+
+void set_path(int op, int path, const char* reason) {
+  if (op < 0 || op >= kPathOps) return;
+  g_path[op] = path;
+  snprintf(g_path_reason[op], sizeof(g_path_reason[op]), "%s", reason ? reason : "");
+}
+
 void set_error(const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -57,6 +67,15 @@ extern "C" {
 int mvb_version(void) { return 100; }
 
 const char* mvb_last_error(void) { return mvb::g_last_error; }
+
+int mvb_last_path(int op, const char** reason) {
+  if (op < 0 || op >= mvb::kPathOps) {
+    if (reason) *reason = "unknown op";
+    return -1;
+  }
+  if (reason) *reason = mvb::g_path_reason[op];
+  return mvb::g_path[op];
+}
 
 int mvb_device_status(int* status) {
   if (status == nullptr) MVB_FAIL(MVB_ERR_ARG, "device_status: null pointer");

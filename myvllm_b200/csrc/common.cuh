@@ -77,6 +77,10 @@ inline void ensure_smem_attr(F* func, int bytes, unsigned long long& mask) {
   }
 }
 
+// Which kernel family the last call of an op ran (mvb_last_path), per host thread.
+// `reason` says why a fallback was taken (NULL/empty for the main path).
+void set_path(int op, int path, const char* reason);
+
 // Host readers of the per-translation-unit device error words (see tcgen05.cuh).
 using StatusReader = int (*)(int*);
 void register_status_reader(StatusReader f);

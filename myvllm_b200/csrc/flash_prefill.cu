@@ -280,7 +280,13 @@ extern "C" int mvb_flash_attention_prefill(const mvb_tensor* q, const mvb_tensor
   p.scale_log2 = scale * 1.4426950408889634f;
   p.bt = nullptr; p.ctx = nullptr; p.sk_b = p.sv_b = p.sbt_s = p.sbt_b = 0; p.block_size = 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (launch_fa_tc(p, q->dtype, head_dim, false, T, T, 0, st) < 0) dispatch_fa<false>(q->dtype, head_dim, p, T, st);
+  const char* why = "";
+  if (launch_fa_tc(p, q->dtype, head_dim, false, T, T, 0, st, &why) < 0) {
+    set_path(MVB_OP_FA_PREFILL, MVB_PATH_MMA_SYNC, why);
+    dispatch_fa<false>(q->dtype, head_dim, p, T, st);
+  } else {
+    set_path(MVB_OP_FA_PREFILL, MVB_PATH_TENSOR_CORE, "");
+  }
   MVB_CHECK_LAUNCH(op);
   return MVB_OK;
 }
@@ -337,7 +343,13 @@ extern "C" int mvb_paged_attention_prefill(const mvb_tensor* q, const mvb_tensor
   p.n_seqs = (int)n_seqs; p.hq = (int)hq; p.hkv = (int)hkv; p.causal = 1;
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (launch_fa_tc(p, q->dtype, (int)d, true, T, 0, k_cache->shape[0], st) < 0) dispatch_fa<true>(q->dtype, (int)d, p, T, st);
+  const char* why = "";
+  if (launch_fa_tc(p, q->dtype, (int)d, true, T, 0, k_cache->shape[0], st, &why) < 0) {
+    set_path(MVB_OP_PAGED_PREFILL, MVB_PATH_MMA_SYNC, why);
+    dispatch_fa<true>(q->dtype, (int)d, p, T, st);
+  } else {
+    set_path(MVB_OP_PAGED_PREFILL, MVB_PATH_TENSOR_CORE, "");
+  }
   MVB_CHECK_LAUNCH(op);
   return MVB_OK;
 }

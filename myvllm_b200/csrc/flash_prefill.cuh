@@ -21,9 +21,10 @@ struct FaParams {
 };
 
 // tcgen05 path: returns -1 when the shape/layout is outside what it handles (the caller then
-// runs the mma.sync kernel), else an MVB status.  T = query tokens, n_blocks = cache blocks.
+// runs the mma.sync kernel; *why names the reason), else an MVB status.  T = query tokens,
+// n_blocks = cache blocks.
 int launch_fa_tc(const FaParams& p, int dtype, int d, bool paged, int64_t T, int64_t n_tokens_kv,
-                 int64_t n_blocks, cudaStream_t st);
+                 int64_t n_blocks, cudaStream_t st, const char** why);
 
 namespace {
 

@@ -396,23 +396,32 @@ bool aligned_stride(int64_t s) { return s % 8 == 0; }
 
 }  // namespace
 
+// Returns -1 (with *why set) when the tensor-core kernel does not take this problem.
 int launch_fa_tc(const FaParams& p, int dtype, int d, bool paged, int64_t T_q, int64_t n_tokens_kv, int64_t n_blocks,
-                 cudaStream_t st) {
-  if (d != 64 && d != 128 && d != 256) return -1;
-  if (dtype != MVB_BF16 && dtype != MVB_F16) return -1;
-  if (!(p.scale_log2 > 0.f)) return -1;  // the softmax folds a positive scale into its FFMA
+                 cudaStream_t st, const char** why) {
+  auto reject = [&](const char* r) {
+    *why = r;
+    return -1;
+  };
+  if (d != 64 && d != 128 && d != 256) return reject("head dim not 64, 128 or 256");
+  if (dtype != MVB_BF16 && dtype != MVB_F16) return reject("dtype not bf16/fp16");
+  if (!(p.scale_log2 > 0.f)) return reject("non-positive softmax scale");  // folded into one FFMA
   // TMA: 16-byte aligned bases and strides; vectorised epilogue: 16-byte output rows
-  if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.o)) return -1;
+  if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.o))
+    return reject("a q/k/v/o base pointer is not 16-byte aligned");
   if (!aligned_stride(p.sq_t) || !aligned_stride(p.sq_h) || !aligned_stride(p.sk_t) || !aligned_stride(p.sk_h) ||
       !aligned_stride(p.sv_t) || !aligned_stride(p.sv_h) || !aligned_stride(p.so_t) || !aligned_stride(p.so_h))
-    return -1;
+    return reject("a token or head stride is not a multiple of 8 elements");
   if (paged) {
     const int bn = fa_tc_bn(d);
     const int bs = p.block_size;
     // a K/V tile is one page segment (bs >= BN) or whole pages of >= 8 rows (bs < BN)
     const bool tiles_ok = bs >= bn ? bs % bn == 0 : (bn % bs == 0 && bs % 8 == 0);
-    if (!tiles_ok || !aligned_stride(p.sk_b) || !aligned_stride(p.sv_b) || n_blocks <= 0) return -1;
+    if (!tiles_ok) return reject("block size does not tile into the kernel's 128-key K/V tiles");
+    if (!aligned_stride(p.sk_b) || !aligned_stride(p.sv_b) || n_blocks <= 0)
+      return reject("cache block stride not a multiple of 8 elements, or an empty cache");
   }
+  *why = "";
   if (dtype == MVB_BF16)
     return paged ? launch_d<__nv_bfloat16, true>(d, p, T_q, n_tokens_kv, n_blocks, st)
                  : launch_d<__nv_bfloat16, false>(d, p, T_q, n_tokens_kv, n_blocks, st);

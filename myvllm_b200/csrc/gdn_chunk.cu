@@ -37,13 +37,22 @@ int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
   int64_t n_seqs = 0;
   int rc = check_gdn(op, q, k, v, g, beta, state, idx, cu, o, &n_seqs);
   if (rc) return rc;
-  if (!chunk_tc_supported(q, k, v, g, beta, state, o))
+  if (!chunk_tc_supported(q, k, v, g, beta, state, o)) {
+    set_path(MVB_OP_CHUNK_GDN, MVB_PATH_SERIAL,
+             "dtype, head size or layout outside the tensor-core kernel (16-bit q/k/v, K = V = 128, "
+             "unit inner strides, 16-byte aligned rows)");
     return run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, gd, st);
+  }
   if (n_seqs == 0 || v->shape[1] == 0) return MVB_OK;
   MVB_CHECK_ARG(ws == nullptr || (ws_bytes >= 8 && (reinterpret_cast<uintptr_t>(ws) & 3) == 0),
                 "%s: workspace must be at least 8 bytes, 4-byte aligned", op);
   rc = launch_chunk_tc(q, k, v, g, beta, state, idx, cu, o, scale, l2norm, n_seqs, static_cast<int*>(ws), gd, st);
-  return rc < 0 ? run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, gd, st) : rc;
+  if (rc < 0) {
+    set_path(MVB_OP_CHUNK_GDN, MVB_PATH_SERIAL, "the TMA descriptors of q/k/v could not be built");
+    return run_recurrent(op, q, k, v, g, beta, state, idx, cu, o, scale, l2norm, gd, st);
+  }
+  set_path(MVB_OP_CHUNK_GDN, MVB_PATH_TENSOR_CORE, "");
+  return rc;
 }
 
 }  // namespace mvb

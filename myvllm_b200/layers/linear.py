@@ -13,6 +13,8 @@ the tensor-parallel size exceeds the number of KV heads (the reference asserts,
 
 from __future__ import annotations
 
+import contextlib
+
 import torch
 import torch.distributed as dist
 import torch.nn.functional as F
@@ -21,10 +23,29 @@ from torch import nn
 from . import comm
 
 
+_tp_override: tuple[int, int] | None = None
+
+
 def tp_rank_size(group=None) -> tuple[int, int]:
+    if _tp_override is not None:
+        return _tp_override
     if dist.is_available() and dist.is_initialized():
         return dist.get_rank(group), dist.get_world_size(group)
     return 0, 1
+
+
+@contextlib.contextmanager
+def tensor_parallel(rank: int, size: int):
+    """Layers constructed inside this block are rank ``rank`` of a ``size``-way split,
+    whatever the process group says; ``tensor_parallel(0, 1)`` builds unsharded layers (no
+    all-reduce) inside a multi-rank job, e.g. a single-rank reference of a sharded model."""
+    global _tp_override
+    prev = _tp_override
+    _tp_override = (int(rank), int(size))
+    try:
+        yield
+    finally:
+        _tp_override = prev
 
 
 class Linear(nn.Module):

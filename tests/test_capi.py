@@ -154,3 +154,21 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA"):
         causal_conv1d_update(x, torch.zeros(8, 4), torch.zeros(2, 3, 8, dtype=torch.bfloat16),
                              torch.zeros(2, dtype=torch.int32))
+
+
+def test_last_path_query():
+    """mvb_last_path answers without a GPU: no call yet on this thread -> "none"; an op id
+    outside the table is rejected."""
+    import threading
+
+    res = {}
+
+    def fresh_thread():  # the record is per host thread, so a new thread starts empty
+        res["paths"] = [_lib.last_path(op) for op in (_lib.OP_CHUNK_GDN, _lib.OP_FA_PREFILL, _lib.OP_PAGED_PREFILL)]
+
+    t = threading.Thread(target=fresh_thread)
+    t.start()
+    t.join()
+    assert res["paths"] == [("none", "")] * 3
+    with pytest.raises(ValueError):
+        _lib.last_path(7)

@@ -42,6 +42,9 @@ def test_varlen_prefill_vs_oracle(d, causal):
 def test_varlen_prefill_c3_full_size_vs_torch_fp32():
     inp = W.c3_inputs(dev)
     o = flash_attention_prefill(inp["q"], inp["k"], inp["v"], inp["cu"], inp["scale"], 16, 2, 256, 256, True)
+    from myvllm_b200 import _lib
+
+    assert _lib.last_path(_lib.OP_FA_PREFILL)[0] == "tensor_core"  # config 3 runs the tcgen05 kernel
     cu = inp["cu"].tolist()
     for s in (0, len(cu) - 2):
         a, b = cu[s], cu[s + 1]

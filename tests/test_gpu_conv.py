@@ -77,3 +77,37 @@ def test_conv_update(width):
     ref = oracle.conv.conv1d_update(to_np(x), to_np(w), st_ref, idx.numpy())
     assert_close(o, ref)
     assert np.array_equal(to_np(st_g), st_ref)
+
+
+def test_conv_fn_c1_channels_short_sequences_permuted_slots():
+    """All 8192 config-1 channels (the conv weight distribution of config 1, non-zero
+    histories) on the edge cases of the state roll (m/ops/causal_conv1d.py:199-218):
+    sequences of 0, 1 and 2 tokens (shorter than W - 1 = 3, so the new state keeps part of
+    the old one), 3 tokens (exactly W - 1), and longer ones, written to permuted slots of a
+    larger cache whose other rows must stay untouched."""
+    lens = [0, 1, 2, 3, 130, 1, 64, 2]
+    g = torch.Generator().manual_seed(31)
+    T, dim, n_slots = sum(lens), W.GDN_CH, 13
+    x = torch.randn(T, dim, generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(dim, W.GDN_W, generator=g)).to(torch.bfloat16)
+    st = torch.randn(n_slots, W.GDN_W - 1, dim, generator=g).to(torch.bfloat16)
+    idx = torch.randperm(n_slots, generator=g)[:len(lens)].to(torch.int32)
+    cu = W.cu_from_lengths(lens, "cpu")
+    st_g = st.to(dev)
+    o = causal_conv1d_fn(x.to(dev), w.to(dev), st_g, idx.to(dev), cu.to(dev))
+    st_ref = to_np(st)
+    ref = oracle.conv.conv1d_fn(to_np(x), to_np(w), st_ref, idx.numpy(), cu.numpy())
+    assert_close(o, ref, what="conv out, all channels")
+    assert np.array_equal(to_np(st_g), st_ref)  # rolled rows and untouched rows, bit for bit
+
+
+def test_conv_update_c2_channels_permuted_slots():
+    """The decode update over all 8192 channels with permuted slots, at config-2 batch."""
+    S, n_slots = 256, 300
+    x, w, st, idx, _ = _case([1] * S, W.GDN_CH, W.GDN_W, torch.bfloat16, seed=77, n_slots=n_slots)
+    st_g = st.to(dev)
+    o = causal_conv1d_update(x.to(dev), w.to(dev), st_g, idx.to(dev))
+    st_ref = to_np(st)
+    ref = oracle.conv.conv1d_update(to_np(x), to_np(w), st_ref, idx.numpy())
+    assert_close(o, ref, what="conv update, all channels")
+    assert np.array_equal(to_np(st_g), st_ref)

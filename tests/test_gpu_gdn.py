@@ -119,6 +119,38 @@ def test_chunk_c1_shapes_vs_fp32_recurrent_kernel():
     assert_state_close(a["state"], b["state"])
 
 
+def test_chunk_tc_full_c1_sequence_vs_oracle():
+    """One full-length config-1 sequence (8192 tokens) through the tensor-core chunk kernel
+    against the oracle (m/ops/gated_delta_rule/gated_delta_rule.py:44-64, restated in
+    float64): q/k/v are the causal conv's bf16 output over the 8192 qkv channels, the q/k
+    L2 norm is fused in the kernel, the gates have the config-1 distributions and the initial
+    state is non-zero.  Five v-heads (both v-heads of k-head 0, and heads of the other k-head
+    groups) are compared: outputs to the bf16 bar, the final state to 1e-3 relative."""
+    from myvllm_b200 import _lib
+    from myvllm_b200.ops.causal_conv1d import causal_conv1d_fn
+
+    inp = W.c1_inputs(dev, seed=0, lengths=[8192])
+    qkv = causal_conv1d_fn(inp["x"], inp["conv_w"], inp["conv_state"], inp["idx"], inp["cu"])
+    q, k, v = W.split_qkv(qkv)
+    g_ = torch.Generator(device=dev).manual_seed(9)
+    state0 = 0.1 * torch.randn(inp["state"].shape, generator=g_, device=dev)
+    state = state0.clone()
+    o = chunk_gated_delta_rule(q, k, v, inp["g"], inp["beta"], state, inp["idx"], inp["cu"],
+                               use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    assert _lib.last_path(_lib.OP_CHUNK_GDN)[0] == "tensor_core"
+    heads = [0, 1, 9, 22, 31]
+    qn, kn = to_np(q), to_np(k)
+    qn = qn / np.sqrt((qn * qn).sum(-1, keepdims=True) + 1e-6)
+    kn = kn / np.sqrt((kn * kn).sum(-1, keepdims=True) + 1e-6)
+    kh = [h // 2 for h in heads]
+    st = to_np(state0)[:, heads]
+    ref = oracle.gdn.chunked(qn[:, kh], kn[:, kh], to_np(v)[:, heads], to_np(inp["g"])[:, heads],
+                             to_np(inp["beta"])[:, heads], st, np.array([0]), inp["cu"].cpu().numpy(), 64)
+    assert_close(o[:, heads], ref, what="o (full C1 sequence)")
+    assert_state_close(state[:, heads], st, what="state (full C1 sequence)")
+
+
 def test_decode_bf16_vs_oracle():
     S, hk, hv = 24, 16, 32
     cpu = _rand_gdn([1] * S, hk, hv, 128, 128, seed=3, n_slots=40)
