@@ -799,8 +799,15 @@ def run_c4(args, rank, world, device):
 def c4_tp_parity(rank, world, device):
     """Two decode steps of a 4-layer slice of the stack (3 GDN + 1 gated attention, 8
     sequences, non-zero states, paged KV) at TP = world, against the same slice built
-    unsharded on rank 0 from the same seeded full weights, states and caches.  The sharded
-    output carries all-reduce rounding, so it is held to the bf16 bar (2e-2 + 1e-2 |ref|)."""
+    unsharded on rank 0 from the same seeded full weights, states and caches.
+
+    The two runs differ only in bf16 rounding: the sharded GEMMs reduce in another order and
+    the all-reduce adds the partial sums, so single activations move by an ulp (2^-8
+    relative), and a GDN decay gate g = -exp(A_log) softplus(a + dt_bias) turns an ulp of
+    its projection `a` into a relative change of the whole state of up to exp(A_log) * 2^-8.
+    The check is therefore normwise: ||out_tp - out_1|| / ||out_1|| <= 1e-2 per step and the
+    same for rank 0's GDN states; a sharding error (a wrong head, channel or KV slice)
+    gives errors of order one."""
     from myvllm_b200 import workloads as W
     from myvllm_b200.decode_stack import HybridDecodeStack, hidden_input
 
@@ -815,16 +822,18 @@ def c4_tp_parity(rank, world, device):
         if rank == 0:
             ref = HybridDecodeStack(4, 8, ctx, 4, device, seed=99, tp=(0, 1))
             routs = [ref.forward(x, *m) for m in ref.step_metadata(2)]
-            errs, ok = [], True
+            rel, mx = [], []
             for a, b in zip(outs, routs):
-                d = (a.float() - b.float()).abs()
-                errs.append(d.max().item())
-                ok = ok and bool((d <= 2e-2 + 1e-2 * b.float().abs()).all().item())
+                a, b = a.float(), b.float()
+                rel.append(((a - b).norm() / b.norm()).item())
+                mx.append((a - b).abs().max().item())
             hv_r = stack.lac.recurrent_cache.shape[2]
             s_a, s_b = stack.lac.recurrent_cache, ref.lac.recurrent_cache[:, :, :hv_r]
-            res = {"check": f"2 decode steps of a 3 GDN + 1 attention slice at tp{world} vs one rank unsharded",
-                   "pass": ok, "max_abs_diff": max(errs),
-                   "state_rel_err_rank0_heads": ((s_a - s_b).norm() / s_b.norm()).item()}
+            s_rel = ((s_a - s_b).norm() / s_b.norm()).item()
+            res = {"check": f"2 decode steps of a 3 GDN + 1 attention slice at tp{world} vs one rank unsharded "
+                            "(normwise relative error <= 1e-2)",
+                   "pass": max(rel) <= 1e-2 and s_rel <= 1e-2, "out_rel_err": rel, "out_max_abs_diff": mx,
+                   "state_rel_err_rank0_heads": s_rel}
             del ref
         torch.distributed.barrier()
     return res
