@@ -13,6 +13,8 @@
  *   mvb_causal_conv1d_fn        m/ops/causal_conv1d.py:221-273       causal_conv1d_fn
  *   mvb_causal_conv1d_update    m/ops/causal_conv1d.py:434-470       causal_conv1d_update
  *   mvb_chunk_gated_delta_rule  m/ops/gated_delta_rule/gated_delta_rule.py:31-66
+ *   mvb_gated_deltanet_decode   m/layers/linear_attention.py:85-123  decode branch of GatedDeltaNet
+ *                               (conv update + l2norm + gates + recurrence + RMSNormGated)
  *   mvb_fused_recurrent_gdn     m/ops/gated_delta_rule/fused_recurrent_gdn.py:105-166
  *                               (also recurrent_gated_delta_rule, gated_delta_rule.py:69-92)
  *   mvb_flash_attention_prefill m/ops/full_attention.py:114-173      flash_attention_prefill
@@ -125,6 +127,23 @@ int mvb_fused_recurrent_gdn_gated(const mvb_tensor* q, const mvb_tensor* k, cons
                                   const mvb_tensor* recurrent_state_indices, mvb_tensor* o, float scale,
                                   int use_qk_l2norm, void* stream);
 
+/* The decode step of a Gated DeltaNet layer in one kernel: causal_conv1d_update (+ SiLU) ->
+ * q/k L2 norm -> in-kernel gates -> recurrent gated delta rule -> RMSNormGated, i.e. the
+ * decode branch of GatedDeltaNet.forward (m/layers/linear_attention.py:85-123, with
+ * RMSNormGated from m/layers/norm.py:44-58), whose separate ops it replaces.
+ * qkv [S, 2 Hk K + Hv V] the input projection's q | k | v channels (16-bit, unit channel
+ * stride, 16-byte aligned rows); conv_weight [conv_dim, W] (2 <= W <= 6); conv_state
+ * [S_max, W-1, conv_dim] and recurrent_state [S_max, Hv, K, V] (fp32), both updated in
+ * place at conv_state_indices / recurrent_state_indices; a, b [S, Hv] raw gate projections;
+ * A_log, dt_bias [Hv]; z [S, Hv, V] the norm's gate; norm_weight [V]; out [S, Hv, V] =
+ * RMSNormGated(o, z).  K = V = 128 and Hv / Hk in {1, 2, 4}; scale <= 0 means K^-0.5. */
+int mvb_gated_deltanet_decode(const mvb_tensor* qkv, const mvb_tensor* conv_weight, mvb_tensor* conv_state,
+                              const mvb_tensor* conv_state_indices, const mvb_tensor* a, const mvb_tensor* b,
+                              const mvb_tensor* a_log, const mvb_tensor* dt_bias, mvb_tensor* recurrent_state,
+                              const mvb_tensor* recurrent_state_indices, const mvb_tensor* z,
+                              const mvb_tensor* norm_weight, float norm_eps, float scale, mvb_tensor* out,
+                              void* stream);
+
 /* Varlen (optionally causal) attention.  q [T, Hq, D]; k [T, Hkv, D]; v [T, Hkv, Dv];
  * cu_seqlens [S+1]; o [T, Hq, Dv] (dtype of q).  bf16/f16 only. */
 int mvb_flash_attention_prefill(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
@@ -144,6 +163,15 @@ int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor* k_cache, c
                                const mvb_tensor* block_tables, const mvb_tensor* context_lens, float scale,
                                int block_size, int64_t max_context_len, mvb_tensor* o, void* workspace,
                                size_t workspace_bytes, void* stream);
+
+/* mvb_paged_attention_decode with the gated-attention output gate applied where o is
+ * written: o = attention * sigmoid(gate), gate [S, Hq, Dv] (dtype of q, unit last stride),
+ * in fp32 with one rounding.  Replaces the decode branch's paged_flash_attention_decode
+ * (m/ops/full_attention.py:282-335) followed by the layer's o * sigmoid(gate). */
+int mvb_paged_attention_decode_gated(const mvb_tensor* q, const mvb_tensor* k_cache, const mvb_tensor* v_cache,
+                                     const mvb_tensor* block_tables, const mvb_tensor* context_lens, float scale,
+                                     int block_size, int64_t max_context_len, const mvb_tensor* gate, mvb_tensor* o,
+                                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Allocation-free variant of mvb_paged_attention_decode (no counterpart in the reference).
  * For callers that may not allocate device memory when they decode: the split-KV partial

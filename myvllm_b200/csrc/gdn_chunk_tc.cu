@@ -23,12 +23,14 @@
 // accumulators fp32 (the final fp32 state stays within 1e-3 relative of the exact recurrence).
 //
 // Two warp groups pipeline consecutive chunks:
-//   prep (warps 0-7): TMA loads, gates, D1, masks, triangular solve, U/W, q'/k', W staging
-//                     for chunk c+1 -- nothing here depends on the state;
-//   rec  (warps 8-11, thread = TMEM lane): Vn, O and the state update for chunk c, the
-//                     output tile and the fp16 state copy for chunk c+1.
-// They hand buffers over through mbarriers (ready / gates-ready from prep; MMA completions
-// and U-buffer releases from rec).  Chains are handed out longest sequence first over a
+//   prep (warps 0-7): TMA loads, gates, D1, masks, triangular solve and the U/W factors for
+//                     chunk c+1 -- nothing here depends on the state;
+//   rec  (warps 8-11, thread = TMEM lane): q'/k', the U/W products and the W staging, then
+//                     Vn, O and the state update for chunk c, the output tile and the fp16
+//                     state copy for chunk c+1.
+// They hand buffers over through mbarriers (normed / factors-ready / gates-ready from prep;
+// MMA completions from rec).  prep publishes chunk c+1 only once the U/W products of chunk
+// c are done, which keeps it at most one phase ahead on every barrier.  Chains are handed out longest sequence first over a
 // persistent grid: dynamically through a work counter when the caller supplies one (the
 // last CTA to run dry zeroes it for the next launch), else round-robin.  Every wait is
 // bounded; a wait that gives up sets the device error word and the CTA winds down.
@@ -91,7 +93,7 @@ struct Params {
 };
 
 struct Bars {
-  uint64_t raw_qk[2], raw_v, d1_done, mma2_done, mma_r, ready, gready[2], r3done, r4done;
+  uint64_t raw_qk[2], raw_v, d1_done, mma2_done, mma_r, gready[2], r4done;
   uint64_t mma2_go, normed, mma_all, mma_all_prep;
 };
 
@@ -333,8 +335,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     umma::mbar_init(&bars.d1_done, 1);
     umma::mbar_init(&bars.mma2_done, 1);
     umma::mbar_init(&bars.mma_r, 1);
-    umma::mbar_init(&bars.ready, 1);
-    umma::mbar_init(&bars.r3done, 1);
     umma::mbar_init(&bars.r4done, 1);
     umma::mbar_fence_init();
   }
@@ -677,30 +677,16 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         if (!(ok = norms(k + 1))) break;
       }
 
-      // ---- U/W done: next loads; stage W^T [kdim][tok] (fp16, MN-major B operand) ----
+      // ---- U/W(k) done: the next loads, then chunk k+1's record.  Publishing only now keeps
+      //      prep one phase ahead at most: rec issued U/W(k) after taking chunk k's record and
+      //      normed phase, so slot (k+1) & 1 and the next normed phase are free ----
       ok = umma::mbar_wait(&bars.mma2_done, k & 1);
       if (tid == 0) v_used = k + 1;
-      if (ok && tid == 0 && k >= 1) ok = umma::mbar_wait(&bars.r3done, (k - 1) & 1);  // W^T buffer free
       if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
-      umma::fence_after();
       if (tid == 0) {
         if (nxt.valid) issue_v(nxt);
         if (nxt2.valid && nxt.valid) issue_qk(nxt2);
       }
-      {
-        float v[32];
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_W + wg * 32), v);
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_W + wg * 32 + 16), v + 16);
-        umma::tmem_wait_ld();
-#pragma unroll
-        for (int cch = 0; cch < 4; ++cch)
-          *reinterpret_cast<uint4*>(sm + SM_WS + umma::sw128(tl, wg * 4 + cch)) = pack8<__half>(v + cch * 8);
-      }
-      umma::fence_async_smem();
-      umma::fence_before();
-      bar_sync(kBarPrep, kPrep);
-      if (tid == 0) tma::arrive(&bars.ready);
-
       if (nxt.valid && !(ok = publish_norms(k + 1, nxt))) break;
       cur = nxt;
       nxt = nxt2;
@@ -761,12 +747,19 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         if (rt < 64) sc = p.scale * exp2f(sFk[F_G + i]) * sFk[F_QN + i];
         else sc = i < recs[b].n ? exp2f(sFk[F_G + C - 1] - sFk[F_G + i]) * sFk[F_KN + i] : 0.f;
         char* dst = sm + (rt < 64 ? SM_QP : SM_KP);
+        // all 16 loads first: the stores below go to other buffers, but the compiler cannot
+        // prove it and would otherwise order every load after the previous store
+        uint4 raw[16];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int c = 0; c < 8; ++c) raw[hh * 8 + c] = *reinterpret_cast<const uint4*>(qk + hh * 16384 + umma::sw128(rt, c));
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             float f[8];
-            unpack8<T>(*reinterpret_cast<const uint4*>(qk + hh * 16384 + umma::sw128(rt, c)), f);
+            unpack8<T>(raw[hh * 8 + c], f);
 #pragma unroll
             for (int j = 0; j < 8; ++j) f[j] *= sc;
             *reinterpret_cast<uint4*>(dst + hh * 8192 + umma::sw128(i, c)) = pack8<__half>(f);
@@ -796,9 +789,23 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       store_o();  // the previous chunk's output tile, while thread 0 issues the MMAs above
       if (!(ok = bar_and(kBarRec, kRec, ok))) break;
 
-      ok = umma::mbar_wait(&bars.ready, k & 1);
+      // ---- U/W done: stage W^T [kdim][tok] (fp16, MN-major B operand of the Vn MMA) ----
+      ok = umma::mbar_wait(&bars.mma2_done, k & 1);
       if (!(ok = bar_and(kBarRec, kRec, ok))) break;
+      umma::fence_after();
+      {
+        float v[64];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_W + q4 * 16), v + q4 * 16);
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int cch = 0; cch < 8; ++cch)
+          *reinterpret_cast<uint4*>(sm + SM_WS + umma::sw128(tl, cch)) = pack8<__half>(v + cch * 8);
+      }
       const Rec rec = recs[b];
+      umma::fence_async_smem();
+      umma::fence_before();
+      bar_sync(kBarRec, kRec);
 
       // ---- chain start: state -> TMEM (pre-scaled by e^{G_last}) and its fp16 copy ----
       if (rec.flags & 2) {
@@ -838,7 +845,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
           umma::mma_f16(tmem + COL_U + b * 64, a_s, umma::desc_mnmajor(sbase + SM_WS, 8192, ks), id_vn, true);
           umma::mma_f16(tmem + COL_O, a_s, umma::desc_kmajor(sbase + SM_QP, 64, ks), id_sq, ks > 0);
         }
-        umma::commit(&bars.r3done);
         umma::commit(&bars.mma_r);
       }
       ok = umma::mbar_wait(&bars.mma_r, ph);
@@ -847,15 +853,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       umma::fence_after();
 
       // ---- stage Vn^T [v][tok] (fp16, K-major) ----
+      {
+        float v[64];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float v[32];
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_U + b * 64 + half * 32), v);
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_U + b * 64 + half * 32 + 16), v + 16);
+        for (int q4 = 0; q4 < 4; ++q4) umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_U + b * 64 + q4 * 16), v + q4 * 16);
         umma::tmem_wait_ld();
 #pragma unroll
-        for (int cch = 0; cch < 4; ++cch)
-          *reinterpret_cast<uint4*>(sm + SM_VN + umma::sw128(tl, half * 4 + cch)) = pack8<__half>(v + cch * 8);
+        for (int cch = 0; cch < 8; ++cch)
+          *reinterpret_cast<uint4*>(sm + SM_VN + umma::sw128(tl, cch)) = pack8<__half>(v + cch * 8);
       }
       umma::fence_async_smem();
       umma::fence_before();
@@ -881,14 +886,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       // ---- epilogue: o tile; fp16 copy of S and S e^{G_last} for the next chunk, or the
       //      final state ----
       T* ot = reinterpret_cast<T*>(sm + SM_O);  // [64 tok][128 v], 2 v-halves of [64][128 B]
+      {
+        float v[64];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float v[32];
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O + half * 32), v);
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O + half * 32 + 16), v + 16);
+        for (int q4 = 0; q4 < 4; ++q4) umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_O + q4 * 16), v + q4 * 16);
         umma::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) ot[umma::elem_off(half * 32 + j, tl, 8192) >> 1] = from_f32<T>(v[j]);
+        for (int j = 0; j < 64; ++j) ot[umma::elem_off(j, tl, 8192) >> 1] = from_f32<T>(v[j]);
       }
       if (rec.flags & 4) {
         float* srow = gstate + (int64_t)tl * p.ss_k;
@@ -905,21 +909,22 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         const int nb = (k + 1) & 1;
         ok = umma::mbar_wait(&bars.gready[nb], ((k + 1) >> 1) & 1);
         const float el = s_el[nb];
-#pragma unroll 2
-        for (int cc = 0; cc < D; cc += 16) {
-          float v[16];
-          const uint32_t a = umma::taddr(tmem, lane_base, COL_S + cc);
-          umma::tmem_ld16(a, v);
+#pragma unroll 1
+        for (int cc = 0; cc < D; cc += 64) {
+          float v[64];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_S + cc + q4 * 16), v + q4 * 16);
           umma::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; j += 8) {
+          for (int j = 0; j < 64; j += 8) {
             const int col = cc + j;
             *reinterpret_cast<uint4*>(sm + SM_S16 + (col >> 6) * 16384 + umma::sw128(tl, (col >> 3) & 7)) =
                 pack8<__half>(v + j);
           }
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] *= el;
-          umma::tmem_st16(a, v);
+          for (int j = 0; j < 64; ++j) v[j] *= el;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) umma::tmem_st16(umma::taddr(tmem, lane_base, COL_S + cc + q4 * 16), v + q4 * 16);
         }
         umma::tmem_wait_st();
       }

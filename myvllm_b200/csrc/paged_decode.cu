@@ -26,6 +26,8 @@ struct DecodeParams {
   const int32_t* bt;
   const int32_t* ctx;
   void* o;
+  const void* gate;  // [S, Hq, Dv] output gate (o *= sigmoid(gate)), or null
+  int64_t sgt_s, sgt_h;
   float* part_o;     // [S, Hkv, n_splits, 16, Dv] fp32, or null when n_splits == 1
   float* part_lse;   // [S, Hkv, n_splits, 16]
   int64_t sq_s, sq_h, so_s, so_h;
@@ -57,6 +59,14 @@ struct DecodeSmem {
 template <int D>
 __device__ __forceinline__ int swz(int r, int c) {
   return r * (D * 2) + ((c ^ (r & 7)) << 4);
+}
+
+// sigmoid(gate[seq, head, c]) of the gated-attention output (fp32 math, one rounding of the
+// product instead of torch's rounding of the sigmoid and of the product).
+template <typename T>
+__device__ __forceinline__ float sigmoid_gate(const DecodeParams& p, int seq, int head, int c) {
+  const float g = to_f32<T>(static_cast<const T*>(p.gate)[(int64_t)seq * p.sgt_s + (int64_t)head * p.sgt_h + c]);
+  return 1.f / (1.f + __expf(-g));
 }
 
 // Block-table entry for token t: from the split's smem copy when it holds it.
@@ -289,7 +299,8 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams 
     const float out = L > 0.f ? O / L : 0.f;
     if (p.n_splits == 1) {
       T* o = static_cast<T*>(p.o);
-      o[seq * p.so_s + (kvh * G + r) * p.so_h + c] = from_f32<T>(out);
+      const float gt = p.gate ? sigmoid_gate<T>(p, seq, kvh * G + r, c) : 1.f;
+      o[seq * p.so_s + (kvh * G + r) * p.so_h + c] = from_f32<T>(out * gt);
     } else {
       const int64_t pi = ((int64_t)seq * p.hkv + kvh) * p.n_splits + split;
       p.part_o[(pi * 16 + r) * D + c] = out;
@@ -326,7 +337,8 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeParams p)
     float acc = 0.f;
     for (int s = 0; s < p.n_splits; ++s)
       if (s_w[s] != 0.f) acc += s_w[s] * p.part_o[((base + s) * 16 + r) * D + c];
-    o[seq * p.so_s + hq * p.so_h + c] = from_f32<T>(tot > 0.f ? acc / tot : 0.f);
+    const float gt = p.gate ? sigmoid_gate<T>(p, seq, hq, c) : 1.f;
+    o[seq * p.so_s + hq * p.so_h + c] = from_f32<T>((tot > 0.f ? acc / tot : 0.f) * gt);
   }
 }
 
@@ -375,7 +387,8 @@ int launch_decode(DecodeParams& p, int64_t n_seqs, cudaStream_t st) {
 // Shared by the workspace and the static-scratch entry points.
 int run_paged_decode(const char* op, const mvb_tensor* q, const mvb_tensor* kc, const mvb_tensor* vc,
                      const mvb_tensor* bt, const mvb_tensor* ctx, float scale, int block_size, int64_t max_ctx,
-                     mvb_tensor* o, void* ws, size_t ws_bytes, int64_t max_splits, cudaStream_t st) {
+                     mvb_tensor* o, void* ws, size_t ws_bytes, int64_t max_splits, cudaStream_t st,
+                     const mvb_tensor* gate = nullptr) {
   int rc;
   if ((rc = check_tensor(q, op, "q", 3)) || (rc = check_tensor(kc, op, "k_cache", 4)) ||
       (rc = check_tensor(vc, op, "v_cache", 4)) || (rc = check_tensor(bt, op, "block_tables", 2)) ||
@@ -409,6 +422,14 @@ int run_paged_decode(const char* op, const mvb_tensor* q, const mvb_tensor* kc, 
   DecodeParams p;
   p.q = q->data; p.kc = kc->data; p.vc = vc->data;
   p.bt = static_cast<const int32_t*>(bt->data); p.ctx = static_cast<const int32_t*>(ctx->data); p.o = o->data;
+  p.gate = nullptr; p.sgt_s = p.sgt_h = 0;
+  if (gate != nullptr) {
+    if ((rc = check_tensor(gate, op, "gate", 3))) return rc;
+    MVB_CHECK_ARG(gate->shape[0] == S && gate->shape[1] == hq && gate->shape[2] == dv && gate->dtype == q->dtype,
+                  "%s: gate must be [S, Hq, Dv] in the dtype of q", op);
+    MVB_CHECK_SUPPORTED(gate->stride[2] == 1, "%s: gate needs a unit last stride", op);
+    p.gate = gate->data; p.sgt_s = gate->stride[0]; p.sgt_h = gate->stride[1];
+  }
   p.sq_s = q->stride[0]; p.sq_h = q->stride[1]; p.so_s = o->stride[0]; p.so_h = o->stride[1];
   p.skc_b = kc->stride[0]; p.skc_t = kc->stride[1]; p.skc_h = kc->stride[2];
   p.svc_b = vc->stride[0]; p.svc_t = vc->stride[1]; p.svc_h = vc->stride[2];
@@ -464,6 +485,17 @@ extern "C" int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor*
   return mvb::run_paged_decode("paged_attention_decode", q, k_cache, v_cache, block_tables, context_lens, scale,
                                block_size, max_context_len, o, workspace, workspace_bytes, mvb::kMaxSplits,
                                static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mvb_paged_attention_decode_gated(const mvb_tensor* q, const mvb_tensor* k_cache,
+                                                const mvb_tensor* v_cache, const mvb_tensor* block_tables,
+                                                const mvb_tensor* context_lens, float scale, int block_size,
+                                                int64_t max_context_len, const mvb_tensor* gate, mvb_tensor* o,
+                                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (gate == nullptr) MVB_FAIL(MVB_ERR_ARG, "paged_attention_decode_gated: gate is NULL");
+  return mvb::run_paged_decode("paged_attention_decode_gated", q, k_cache, v_cache, block_tables, context_lens,
+                               scale, block_size, max_context_len, o, workspace, workspace_bytes, mvb::kMaxSplits,
+                               static_cast<cudaStream_t>(stream), gate);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -97,7 +97,9 @@ class GatedAttention(nn.Module):
                 o = flash_attention_prefill(q, k, v, ctx.cu_seqlens_q, self.scale, self.num_q_heads,
                                             self.num_kv_heads, D, Dv, True)
         else:
+            # the output gate is applied where the decode kernel writes o
             o = paged_flash_attention_decode(q, self.k_cache, self.v_cache, ctx.block_tables, ctx.context_lens,
-                                             self.scale, ctx.block_size)
+                                             self.scale, ctx.block_size, output_gate=gate)
+            return self.o_proj(o.reshape(T, self.num_q_heads * Dv))
         o = o * torch.sigmoid(gate)
         return self.o_proj(o.reshape(T, self.num_q_heads * Dv))

@@ -27,6 +27,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops.causal_conv1d import causal_conv1d_fn, causal_conv1d_update
+from ..ops.gated_delta_rule.fused_layer import fused_decode_supported, gated_deltanet_decode
 from ..ops.gated_delta_rule.gated_delta_rule import chunk_gated_delta_rule, recurrent_gated_delta_rule
 from .linear import ColumnParallelLinear, QKVParallelLinear, RowParallelLinear, tp_rank_size
 from .norm import RMSNormGated
@@ -89,6 +90,14 @@ class GatedDeltaNet(nn.Module):
             qkv, z = self.in_proj_qkv(x), self.in_proj_z(x)
             a, b = self.in_proj_a(x), self.in_proj_b(x)
         gate_inputs = (a, b, self.A_log, self.dt_bias)  # g, beta are formed inside the kernel
+        zv = z.view(T, self.num_v_heads, self.v_head_dim)
+        if not is_prefill and fused_decode_supported(qkv, self.recurrent_state, self.num_k_heads, self.num_v_heads,
+                                                     zv):
+            # conv update + q/k norm + gates + recurrence + RMSNormGated in one kernel
+            o = gated_deltanet_decode(qkv, self.conv1d.weight, self.conv_state, conv_state_indices, a, b, self.A_log,
+                                      self.dt_bias, self.recurrent_state, recurrent_state_indices, zv,
+                                      self.norm.weight, self.norm.variance_epsilon)
+            return self.out_proj(o.reshape(T, self.v_size))
         if is_prefill:
             qkv = causal_conv1d_fn(qkv, self.conv1d.weight, self.conv_state, conv_state_indices, cu_seqlens)
         else:
@@ -103,5 +112,5 @@ class GatedDeltaNet(nn.Module):
         else:
             o = recurrent_gated_delta_rule(q, k, v, None, None, self.recurrent_state, recurrent_state_indices,
                                            use_qk_l2norm_in_kernel=True, gate_inputs=gate_inputs)
-        o = self.norm(o, z.view(T, self.num_v_heads, self.v_head_dim))
+        o = self.norm(o, zv)
         return self.out_proj(o.reshape(T, self.v_size))

@@ -46,7 +46,12 @@ def paged_flash_attention_decode(
     scale: float,
     block_size: int,
     max_context_len: int | None = None,
+    *,
+    output_gate: torch.Tensor | None = None,
 ) -> torch.Tensor:
+    """``output_gate`` [seq_cnt, num_q_heads, v_head_dim] (optional, additive to the reference
+    signature): returns ``o * sigmoid(output_gate)``, the gated attention's output gate applied
+    where the kernel writes o."""
     _lib.require_cuda("paged_flash_attention_decode", q, k_cache, v_cache, block_tables, context_lens)
     seq_cnt, num_q_heads, _ = q.shape
     num_kv_heads, v_head_dim = v_cache.shape[-2:]
@@ -54,6 +59,13 @@ def paged_flash_attention_decode(
     bound = int(max_context_len) if max_context_len else int(block_tables.shape[1]) * int(block_size)
     nbytes = _lib.load().mvb_paged_attention_decode_workspace_size(seq_cnt, num_kv_heads, v_head_dim, bound)
     ws = _lib.workspace(q.device, nbytes, tag="paged_decode") if nbytes else None
+    if output_gate is not None:
+        _lib.require_cuda("paged_flash_attention_decode", output_gate)
+        _lib.call("paged_flash_attention_decode", "mvb_paged_attention_decode_gated", _lib.desc(q),
+                  _lib.desc(k_cache), _lib.desc(v_cache), _lib.desc(_i32(block_tables)), _lib.desc(_i32(context_lens)),
+                  float(scale), int(block_size), bound, _lib.desc(output_gate), _lib.desc(o),
+                  ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, _lib.stream_of(q))
+        return o
     _lib.call("paged_flash_attention_decode", "mvb_paged_attention_decode", _lib.desc(q), _lib.desc(k_cache),
               _lib.desc(v_cache), _lib.desc(_i32(block_tables)), _lib.desc(_i32(context_lens)), float(scale),
               int(block_size), bound, _lib.desc(o), ws.data_ptr() if ws is not None else None,

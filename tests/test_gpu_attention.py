@@ -213,3 +213,20 @@ def test_varlen_prefill_fp16_and_strided_q(d):
                                 qkv_d[:, (hq + hkv) * d:].view(T, hkv, d), cu.to(dev), d ** -0.5, hq, hkv, d, d, True)
     ref = oracle.attention.varlen(to_np(q), to_np(k), to_np(v), cu.numpy(), d ** -0.5, True)
     assert_close(o, ref)
+
+
+@pytest.mark.parametrize("ctx_lens", [[3000, 17, 256, 8000], [1, 40]])
+def test_paged_decode_output_gate(ctx_lens):
+    """mvb_paged_attention_decode_gated: the gated attention's o * sigmoid(gate) applied in the
+    decode kernel (split and unsplit paths) against the plain decode times a torch sigmoid;
+    the gate is a strided view, as the layer slices it from its fused projection."""
+    kc, vc, bt = _paged(ctx_lens, 2, 256, 256, seed=12, device=dev)
+    g = torch.Generator(device=dev).manual_seed(13)
+    q = torch.randn(len(ctx_lens), 16, 256, generator=g, device=dev).to(torch.bfloat16)
+    qg = torch.randn(len(ctx_lens), 16, 512, generator=g, device=dev).to(torch.bfloat16)
+    gate = qg[..., 256:]  # row strides 8192 / 512, as in [q | gate] per head
+    ctx = torch.tensor(ctx_lens, dtype=torch.int32, device=dev)
+    plain = paged_flash_attention_decode(q, kc, vc, bt.to(dev), ctx, 1 / 16, 256)
+    gated = paged_flash_attention_decode(q, kc, vc, bt.to(dev), ctx, 1 / 16, 256, output_gate=gate)
+    ref = plain.float() * torch.sigmoid(gate.float())
+    assert_close(gated, ref, what="gated decode")

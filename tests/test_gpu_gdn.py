@@ -276,3 +276,45 @@ def test_gated_entry_points_match_torch_gates(prefill):
                                         gate_inputs=(a, b, a_log, dt_bias))
     assert_close(o2, o1, what="output")
     assert ((s2 - s1).norm() / s1.norm()).item() < 1e-5
+
+
+@pytest.mark.parametrize("hk,hv", [(16, 32), (4, 4), (2, 8)])
+def test_fused_layer_decode_matches_the_unfused_ops(hk, hv):
+    """mvb_gated_deltanet_decode (conv update + q/k norm + gates + recurrence + RMSNormGated in
+    one kernel) against the same layer step run as the separate library ops the layer used
+    before: the conv and recurrent states must come out bit for bit equal (same arithmetic),
+    the normed output within the bf16 bar.  Hv / Hk = 2 (the config-2/4 layout), 1 and 4;
+    permuted state slots; projection rows taken as strided views of one fused GEMM output."""
+    from myvllm_b200.layers.norm import RMSNormGated
+    from myvllm_b200.ops.causal_conv1d import causal_conv1d_update
+    from myvllm_b200.ops.gated_delta_rule.fused_layer import gated_deltanet_decode
+
+    S, n_slots, K = 64, 80, 128
+    conv_dim = 2 * hk * K + hv * K
+    g_ = torch.Generator(device=dev).manual_seed(hk * 100 + hv)
+    fused_out = torch.randn(S, conv_dim + hv * K + 2 * hv, generator=g_, device=dev).to(torch.bfloat16)
+    qkv = fused_out[:, :conv_dim]
+    z = fused_out[:, conv_dim:conv_dim + hv * K].view(S, hv, K)
+    a = fused_out[:, conv_dim + hv * K:conv_dim + hv * K + hv]
+    b = fused_out[:, conv_dim + hv * K + hv:]
+    w = (0.3 * torch.randn(conv_dim, 4, generator=g_, device=dev)).to(torch.bfloat16)
+    conv0 = torch.randn(n_slots, 3, conv_dim, generator=g_, device=dev).to(torch.bfloat16)
+    st0 = 0.1 * torch.randn(n_slots, hv, K, K, generator=g_, device=dev)
+    A_log = torch.empty(hv, device=dev).uniform_(0, np.log(16), generator=g_)
+    dt_bias = 0.1 * torch.randn(hv, generator=g_, device=dev)
+    idx = torch.randperm(n_slots, generator=torch.Generator().manual_seed(3))[:S].to(torch.int32).to(dev)
+    norm = RMSNormGated((K,), 1e-6).to(dev, torch.bfloat16)
+    norm.weight.data.copy_(1 + 0.1 * torch.randn(K, generator=g_, device=dev))
+
+    c1, s1 = conv0.clone(), st0.clone()
+    out = gated_deltanet_decode(qkv, w, c1, idx, a, b, A_log, dt_bias, s1, idx, z, norm.weight, 1e-6)
+    c2, s2 = conv0.clone(), st0.clone()
+    xc = causal_conv1d_update(qkv, w, c2, idx)
+    q, k, v = W.split_qkv(xc, hk, hv, K, K)
+    o = fused_recurrent_gdn(q, k, v, None, None, s2, idx, use_qk_l2norm_in_kernel=True,
+                            gate_inputs=(a, b, A_log, dt_bias))
+    ref = norm(o, z)
+    torch.cuda.synchronize()
+    assert torch.equal(c1, c2), "conv state differs from the unfused conv update"
+    assert torch.equal(s1, s2), "recurrent state differs from the unfused recurrence"
+    assert_close(out, ref, what="fused decode output")
