@@ -577,6 +577,22 @@ def run_c2(args, rank, world, device):
         clocks = clk.summary()
     check_device("c2")
     rec_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evs), world)
+    # the same decode step as the layer runs it: one kernel for conv update + q/k norm + gates
+    # + recurrence + RMSNormGated (the norm's gate z and weight added)
+    from myvllm_b200.ops.gated_delta_rule.fused_layer import gated_deltanet_decode
+
+    gz = torch.Generator(device=device).manual_seed(5)
+    z = torch.randn(inp["x"].shape[0], W.GDN_HV, W.GDN_DV, generator=gz, device=device).to(torch.bfloat16)
+    nw = torch.ones(W.GDN_DV, device=device, dtype=torch.bfloat16)
+
+    def fused_step(i=None):
+        return gated_deltanet_decode(inp["x"], inp["conv_w"], inp["conv_state"], inp["idx"], inp["a"], inp["b"],
+                                     inp["A_log"], inp["dt_bias"], inp["state"], inp["idx"], z, nw, 1e-6)
+
+    for _ in range(args.warmup):
+        fused_step()
+    fused_ms = timed_region(fused_step, n, world)
+    check_device("c2 fused")
     host_in = {k: inp[k].cpu().pin_memory() for k in ("x", "g", "beta")}
     o_host = torch.empty(inp["x"].shape[0], W.GDN_HV, W.GDN_DV, dtype=torch.bfloat16).pin_memory()
     e2e_ms = _serial_e2e(step, host_in, inp, o_host, 20, world)
@@ -605,6 +621,11 @@ def run_c2(args, rank, world, device):
                     "d2h_bytes_per_step": o_host.numel() * 2, "steps": 20,
                     "pipeline": "per step: H2D of the step's qkv projection and gates (pinned) -> conv update + "
                                 "recurrent GDN -> D2H of o; states stay resident"},
+            "fused_layer_step": {"us": fused_ms * 1e3, "steps": n, "kernel": "gdn_decode_fused_kernel",
+                                 "what": "conv update + q/k L2 norm + gates + recurrence + RMSNormGated in one "
+                                         "kernel (mvb_gated_deltanet_decode), as GatedDeltaNet decodes",
+                                 "hbm_frac": (step_bytes + 2 * z.numel() * 2) / (fused_ms * 1e-3) / 1e9
+                                 / pk["hbm_gbs"]},
             "gpu_launches": 2 * n, "device_status": 0, "clocks": clocks}
 
 

@@ -13,6 +13,8 @@
  *   mvb_causal_conv1d_fn        m/ops/causal_conv1d.py:221-273       causal_conv1d_fn
  *   mvb_causal_conv1d_update    m/ops/causal_conv1d.py:434-470       causal_conv1d_update
  *   mvb_chunk_gated_delta_rule  m/ops/gated_delta_rule/gated_delta_rule.py:31-66
+ *   mvb_gated_deltanet_prefill  m/layers/linear_attention.py:107-121 chunk GDN + RMSNormGated of the
+ *                               prefill branch (gates, q/k norm and output norm in the kernel)
  *   mvb_gated_deltanet_decode   m/layers/linear_attention.py:85-123  decode branch of GatedDeltaNet
  *                               (conv update + l2norm + gates + recurrence + RMSNormGated)
  *   mvb_fused_recurrent_gdn     m/ops/gated_delta_rule/fused_recurrent_gdn.py:105-166
@@ -143,6 +145,19 @@ int mvb_gated_deltanet_decode(const mvb_tensor* qkv, const mvb_tensor* conv_weig
                               const mvb_tensor* recurrent_state_indices, const mvb_tensor* z,
                               const mvb_tensor* norm_weight, float norm_eps, float scale, mvb_tensor* out,
                               void* stream);
+
+/* The prefill branch of a Gated DeltaNet layer after its conv: mvb_chunk_gated_delta_rule_gated
+ * with the q/k L2 norm on and RMSNormGated(o, z) (m/layers/norm.py:44-58) applied to each
+ * output tile before it is stored, i.e. GatedDeltaNet.forward's chunk_gated_delta_rule +
+ * self.norm (m/layers/linear_attention.py:107-121).  Arguments as mvb_chunk_gated_delta_rule_gated,
+ * plus z [T, Hv, V] (dtype of v, 16-byte aligned rows) and norm_weight [V]; out [T, Hv, V].
+ * Needs the tensor-core layout (16-bit q/k/v, K = V = 128); MVB_ERR_UNSUPPORTED otherwise. */
+int mvb_gated_deltanet_prefill(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* a,
+                               const mvb_tensor* b, const mvb_tensor* a_log, const mvb_tensor* dt_bias,
+                               mvb_tensor* recurrent_state, const mvb_tensor* recurrent_state_indices,
+                               const mvb_tensor* cu_seqlens, const mvb_tensor* z, const mvb_tensor* norm_weight,
+                               float norm_eps, mvb_tensor* out, float scale, void* workspace, size_t workspace_bytes,
+                               void* stream);
 
 /* Varlen (optionally causal) attention.  q [T, Hq, D]; k [T, Hkv, D]; v [T, Hkv, Dv];
  * cu_seqlens [S+1]; o [T, Hq, Dv] (dtype of q).  bf16/f16 only. */

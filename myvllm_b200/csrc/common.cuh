@@ -131,6 +131,16 @@ struct GateDev {
   int alog_dt = 0, dtb_dt = 0;
 };
 
+// RMSNormGated applied to a GDN output (m/layers/norm.py:44-58): out = o rsqrt(mean(o^2) +
+// eps) w silu(z) over the V axis; z [T, Hv, V] (strides z_t, z_h, unit last stride), w [V].
+struct NormDev {
+  const void* z = nullptr;  // null: no norm
+  int64_t z_t = 0, z_h = 0;
+  const void* w = nullptr;
+  int w_dt = 0;
+  float eps = 0.f;
+};
+
 __device__ __forceinline__ float load_scalar(const void* p, int64_t i, int dtype) {
   if (dtype == MVB_F32) return static_cast<const float*>(p)[i];
   if (dtype == MVB_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);

@@ -23,13 +23,13 @@
 // accumulators fp32 (the final fp32 state stays within 1e-3 relative of the exact recurrence).
 //
 // Two warp groups pipeline consecutive chunks:
-//   prep (warps 0-7): TMA loads, gates, D1, masks, triangular solve and the U/W factors for
-//                     chunk c+1 -- nothing here depends on the state;
-//   rec  (warps 8-11, thread = TMEM lane): q'/k', the U/W products and the W staging, then
-//                     Vn, O and the state update for chunk c, the output tile and the fp16
-//                     state copy for chunk c+1.
+//   prep (warps 0-7): TMA loads, gates, D1, the mask of A, triangular solve and the U/W
+//                     factors for chunk c+1 -- nothing here depends on the state;
+//   rec  (warps 8-11, thread = TMEM lane): q'/k', Aqk, the U/W products and the W staging,
+//                     then Vn, O and the state update for chunk c, the output tile and the
+//                     fp16 state copy for chunk c+1.
 // They hand buffers over through mbarriers (normed / factors-ready / gates-ready from prep;
-// MMA completions from rec).  prep publishes chunk c+1 only once the U/W products of chunk
+// MMA completions and D1-read from rec).  prep publishes chunk c+1 only once the U/W products of chunk
 // c are done, which keeps it at most one phase ahead on every barrier.  Chains are handed out longest sequence first over a
 // persistent grid: dynamically through a work counter when the caller supplies one (the
 // last CTA to run dry zeroes it for the next launch), else round-robin.  Every wait is
@@ -90,10 +90,11 @@ struct Params {
   int n_seqs, hk, hv, l2norm, g32, b32;
   float scale;
   GateDev gd;  // raw gates (a, b in the g, beta slots) when gd.alog is set
+  NormDev nd;  // RMSNormGated on the output tile when nd.z is set
 };
 
 struct Bars {
-  uint64_t raw_qk[2], raw_v, d1_done, mma2_done, mma_r, gready[2], r4done;
+  uint64_t raw_qk[2], raw_v, d1_done, mma2_done, mma_r, gready[2], r4done, aqk_done;
   uint64_t mma2_go, normed, mma_all, mma_all_prep;
 };
 
@@ -336,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     umma::mbar_init(&bars.mma2_done, 1);
     umma::mbar_init(&bars.mma_r, 1);
     umma::mbar_init(&bars.r4done, 1);
+    umma::mbar_init(&bars.aqk_done, 1);
     umma::mbar_fence_init();
   }
   if (warp == 0) umma::tmem_alloc(&tmem_slot, TMEM_COLS);
@@ -465,11 +467,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       }
     };
     // raw tile of chunk kk landed -> D1 = [q; k] k^T on the tensor core (the D1 tile of chunk
-    // kk-1 has been read: its mask and Aqk precede this call) -> q/k norms (and
-    // G - log2(1/|k|) per k column)
+    // kk-1 has been read: its mask precedes this call, its Aqk is awaited below) -> q/k norms
+    // (and G - log2(1/|k|) per k column)
     auto norms = [&](int kk) -> bool {
       bool w = umma::mbar_wait(&bars.raw_qk[kk & 1], (kk >> 1) & 1);
       if (tid == 0) qk_used = kk + 1;
+      // rec has read D1 of chunk kk-1 (its Aqk) before this chunk's D1 overwrites it
+      if (tid == 0 && kk >= 1) w = w && umma::mbar_wait(&bars.aqk_done, (kk - 1) & 1);
       if (!(w = bar_and(kBarPrep, kPrep, w))) return false;
       const char* qk = sm + SM_QK + (kk & 1) * 32768;
       if (tid == 0) {
@@ -601,11 +605,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       // ---- Ti = (I + A)^-1 ----
       solve_tril64(sm + SM_A, sm + SM_A + 8192, reinterpret_cast<const float*>(sm + SM_AD), sm + SM_T,
                    sm + SM_T + 8192, tid);
-      if (tid == 0 && k >= 1) ok = umma::mbar_wait(&bars.r4done, (k - 1) & 1);  // Aqk buffer free
-      if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
 
       // ---- U/W factors split hi + lo in the input type (they overwrite Ti: read all, then
-      //      write); Aqk (fp16) from the q rows of D1 ----
+      //      write) ----
       {
         uint4 fo[2][4];
 #pragma unroll
@@ -639,29 +641,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
           for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(sm + SM_TF + q * 8192 + off) = fo[it][q];
         }
       }
-      if (tl < 64) {
-        float v[32];
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
-        const int i = tl;
-        const float rowf = p.scale * sFk[F_QN + i];
-        const float gi = sFk[F_G + i];
-        float gc[32];
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const float4 x = *reinterpret_cast<const float4*>(sFk + F_GC + wg * 32 + 4 * m);
-          gc[4 * m] = x.x; gc[4 * m + 1] = x.y; gc[4 * m + 2] = x.z; gc[4 * m + 3] = x.w;
-        }
-        umma::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float e = ex2(gi - gc[j]);
-          v[j] = wg * 32 + j <= i ? rowf * v[j] * e : 0.f;
-        }
-#pragma unroll
-        for (int cch = 0; cch < 4; ++cch)
-          *reinterpret_cast<uint4*>(sm + SM_AQK + umma::sw128(i, wg * 4 + cch)) = pack8<__half>(v + cch * 8);
-      }
       umma::fence_async_smem();
       umma::fence_before();
       bar_sync(kBarPrep, kPrep);
@@ -670,6 +649,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       if (tid == 0) tma::arrive(&bars.mma2_go);
 
       // ---- meanwhile: gates and norms of chunk k+1 (once rec has read chunk k's) ----
+      // (gates(k+1) rewrites the gate slot of chunk k-1, which rec reads until it issues the
+      // output/state MMAs of that chunk)
+      if (tid == 0 && k >= 1) ok = umma::mbar_wait(&bars.r4done, (k - 1) & 1);
+      if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
       Item nxt2 = nxt;
       if (nxt.valid) {
         nxt2 = next_item(nxt);
@@ -722,13 +705,38 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     const uint32_t id_s = umma::idesc_f16(128, 128, true, false);
     // deferred store of the last output tile (o tile in SM_O; pend_n == 0: nothing pending)
     int pend_c0 = 0, pend_h = 0, pend_n = 0;
+    // The 16 lanes of a half warp store one token row (16 x 8 columns); with the layer's
+    // output norm they first form its RMS over the 128 columns by a 4-step shuffle and apply
+    // RMSNormGated to the rounded tile, as the reference applies it to the op's output.
+    const bool norm = p.nd.z != nullptr;
+    float nw8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) nw8[j] = norm ? load_scalar(p.nd.w, (rt & 15) * 8 + j, p.nd.w_dt) : 1.f;
     auto store_o = [&]() {
       for (int e = rt; e < C * 16; e += kRec) {
         const int i = e >> 4, c16 = e & 15;
-        if (i < pend_n) {
-          const uint4 val = *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7));
-          *reinterpret_cast<uint4*>(go + (int64_t)(pend_c0 + i) * p.so_t + (int64_t)pend_h * p.so_h + c16 * 8) = val;
+        const bool live = i < pend_n;
+        uint4 val = live ? *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7))
+                         : make_uint4(0, 0, 0, 0);
+        if (norm) {  // uniform: every lane takes part in the shuffles
+          float f[8], zf[8];
+          unpack8<T>(val, f);
+          float ss = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+#pragma unroll
+          for (int off = 1; off < 16; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+          if (live) {
+            const float r = rsqrtf(ss / (float)D + p.nd.eps);
+            unpack8<T>(*reinterpret_cast<const uint4*>(static_cast<const T*>(p.nd.z) + (int64_t)(pend_c0 + i) * p.nd.z_t +
+                                                       (int64_t)pend_h * p.nd.z_h + c16 * 8),
+                       zf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = f[j] * r * nw8[j] * silu(zf[j]);
+            val = pack8<T>(f);
+          }
         }
+        if (live) *reinterpret_cast<uint4*>(go + (int64_t)(pend_c0 + i) * p.so_t + (int64_t)pend_h * p.so_h + c16 * 8) = val;
       }
       pend_n = 0;
     };
@@ -765,8 +773,35 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
             *reinterpret_cast<uint4*>(dst + hh * 8192 + umma::sw128(i, c)) = pack8<__half>(f);
           }
       }
+      // ---- Aqk = lower(scale D1[q] e^{G_i - G_j} / |q_i||k_j|) (fp16) from the q rows of D1
+      //      (TMEM lanes 0-63: warps 8 and 9, one row each, all 64 columns) ----
+      if (rt < 64) {
+        const float* sFk = sF + b * kFSet;
+        float v[64];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + q4 * 16), v + q4 * 16);
+        const int i = rt;
+        const float rowf = p.scale * sFk[F_QN + i];
+        const float gi = sFk[F_G + i];
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int q4 = 0; q4 < 16; ++q4) {
+          const float4 x = *reinterpret_cast<const float4*>(sFk + F_GC + 4 * q4);
+          const float gc[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int col = q4 * 4 + j;
+            v[col] = col <= i ? rowf * v[col] * ex2(gi - gc[j]) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int cch = 0; cch < 8; ++cch)
+          *reinterpret_cast<uint4*>(sm + SM_AQK + umma::sw128(i, cch)) = pack8<__half>(v + cch * 8);
+      }
       umma::fence_async_smem();
+      umma::fence_before();
       bar_sync(kBarRec, kRec);
+      if (rt == 0) tma::arrive(&bars.aqk_done);
 
       // ---- U^T = v^T (Tu_hi + Tu_lo)^T, W^T = k^T (Tw_hi + Tw_lo)^T once prep has the factors ----
       if (rt == 0) {
@@ -974,7 +1009,7 @@ bool chunk_tc_supported(const mvb_tensor* q, const mvb_tensor* k, const mvb_tens
 int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
                     const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
                     mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, const GateDev& gd,
-                    cudaStream_t st) {
+                    cudaStream_t st, const NormDev& nd) {
   Params p;
   memset(&p, 0, sizeof(p));
   const int64_t T_tok = q->shape[0];
@@ -997,6 +1032,7 @@ int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* 
   p.l2norm = l2norm ? 1 : 0; p.g32 = g->dtype == MVB_F32; p.b32 = beta->dtype == MVB_F32;
   p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   p.gd = gd;
+  p.nd = nd;
   const int chains = (int)(n_seqs * p.hv);
   const int grid = chains < num_sms() ? chains : num_sms();
   if (q->dtype == MVB_BF16) {

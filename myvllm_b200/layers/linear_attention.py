@@ -27,7 +27,8 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops.causal_conv1d import causal_conv1d_fn, causal_conv1d_update
-from ..ops.gated_delta_rule.fused_layer import fused_decode_supported, gated_deltanet_decode
+from ..ops.gated_delta_rule.fused_layer import (fused_decode_supported, fused_prefill_supported,
+                                                 gated_deltanet_decode, gated_deltanet_prefill)
 from ..ops.gated_delta_rule.gated_delta_rule import chunk_gated_delta_rule, recurrent_gated_delta_rule
 from .linear import ColumnParallelLinear, QKVParallelLinear, RowParallelLinear, tp_rank_size
 from .norm import RMSNormGated
@@ -106,6 +107,12 @@ class GatedDeltaNet(nn.Module):
         q = q.view(T, self.num_k_heads, self.k_head_dim)
         k = k.view(T, self.num_k_heads, self.k_head_dim)
         v = v.view(T, self.num_v_heads, self.v_head_dim)
+        if is_prefill and fused_prefill_supported(q, k, v, self.recurrent_state, zv):
+            # chunked GDN with the gates, the q/k norm and RMSNormGated in the kernel
+            o = gated_deltanet_prefill(q, k, v, a, b, self.A_log, self.dt_bias, self.recurrent_state,
+                                       recurrent_state_indices, cu_seqlens, zv, self.norm.weight,
+                                       self.norm.variance_epsilon)
+            return self.out_proj(o.reshape(T, self.v_size))
         if is_prefill:
             o = chunk_gated_delta_rule(q, k, v, None, None, self.recurrent_state, recurrent_state_indices, cu_seqlens,
                                        use_qk_l2norm_in_kernel=True, gate_inputs=gate_inputs)

@@ -44,3 +44,35 @@ def gated_deltanet_decode(qkv, conv_weight, conv_state, conv_state_indices, a, b
               _lib.desc(dt_bias), _lib.desc(recurrent_state), _lib.desc(ridx), _lib.desc(z),
               _lib.desc(norm_weight), float(norm_eps), scale, _lib.desc(out), _lib.stream_of(qkv))
     return out
+
+
+def fused_prefill_supported(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, recurrent_state: torch.Tensor,
+                            z: torch.Tensor) -> bool:
+    """Layouts the tensor-core chunk kernel takes (16-bit q/k/v with K = V = 128, unit inner
+    strides, 16-byte aligned rows), with a 16-byte aligned z of v's shape and dtype."""
+    def rows16(t):
+        return t.stride(-1) == 1 and all(s % 8 == 0 for s in t.stride()[:-1]) and t.data_ptr() % 16 == 0
+
+    return (q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and q.shape[-1] == 128 and v.shape[-1] == 128
+            and all(rows16(t) for t in (q, k, v, z)) and z.shape == v.shape and z.dtype == v.dtype
+            and recurrent_state.dtype == torch.float32 and recurrent_state.stride(-1) == 1)
+
+
+def gated_deltanet_prefill(q, k, v, a, b, A_log, dt_bias, recurrent_state, recurrent_state_indices, cu_seqlens, z,
+                           norm_weight, norm_eps: float) -> torch.Tensor:
+    """The prefill branch of GatedDeltaNet after its conv: chunked gated delta rule with the q/k
+    L2 norm and the gates formed in the kernel, and RMSNormGated(o, z) applied to each output
+    tile before it is stored (``mvb_gated_deltanet_prefill``).  q, k [T, Hk, K]; v, z
+    [T, Hv, V]; a, b [T, Hv]; recurrent_state [S_max, Hv, K, V] fp32, read at and written back
+    to recurrent_state_indices; returns [T, Hv, V]."""
+    _lib.require_cuda("gated_deltanet_prefill", q, k, v, a, b, A_log, dt_bias, recurrent_state,
+                      recurrent_state_indices, cu_seqlens, z, norm_weight)
+    idx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
+    cu = cu_seqlens if cu_seqlens.dtype == torch.int32 else cu_seqlens.int()
+    out = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    ws = _lib.workspace(q.device, 8, tag="gdn_chunk")  # work counter of the dynamic scheduler
+    _lib.call("gated_deltanet_prefill", "mvb_gated_deltanet_prefill", _lib.desc(q), _lib.desc(k), _lib.desc(v),
+              _lib.desc(a), _lib.desc(b), _lib.desc(A_log), _lib.desc(dt_bias), _lib.desc(recurrent_state),
+              _lib.desc(idx), _lib.desc(cu), _lib.desc(z), _lib.desc(norm_weight), float(norm_eps), _lib.desc(out),
+              float(k.shape[-1] ** -0.5), ws.data_ptr(), ws.numel(), _lib.stream_of(q))
+    return out

@@ -105,7 +105,8 @@ def c2_inputs(device, seed: int = 0, n_seqs: int = 256, dtype=torch.bfloat16):
     b = torch.randn(S, GDN_HV, generator=g_).to(device)
     g, beta = gdn_gates(a, b, A_log, dt_bias)
     idx = torch.randperm(S, generator=g_).to(device=device, dtype=torch.int32)
-    return dict(x=x, conv_w=conv_w, conv_state=conv_state, g=g, beta=beta, state=state, idx=idx)
+    return dict(x=x, conv_w=conv_w, conv_state=conv_state, g=g, beta=beta, state=state, idx=idx, a=a, b=b,
+                A_log=A_log, dt_bias=dt_bias)
 
 
 def c3_inputs(device, seed: int = 0, lengths=None, dtype=torch.bfloat16, block_size: int = 256, n_seqs: int = 8):

@@ -318,3 +318,40 @@ def test_fused_layer_decode_matches_the_unfused_ops(hk, hv):
     assert torch.equal(c1, c2), "conv state differs from the unfused conv update"
     assert torch.equal(s1, s2), "recurrent state differs from the unfused recurrence"
     assert_close(out, ref, what="fused decode output")
+
+
+def test_fused_layer_prefill_matches_the_unfused_ops():
+    """mvb_gated_deltanet_prefill (chunk GDN with in-kernel gates and q/k norm, RMSNormGated
+    applied to each output tile) against the chunk op followed by the RMSNormGated op: the
+    final states bit for bit (the norm does not touch them), the normed output within the
+    bf16 bar.  Ragged sequences (partial last chunks) and permuted state slots."""
+    from myvllm_b200.layers.norm import RMSNormGated
+    from myvllm_b200.ops.gated_delta_rule.fused_layer import gated_deltanet_prefill
+
+    lens = [1, 63, 64, 65, 300, 129]
+    hk, hv, K = 4, 8, 128
+    T = sum(lens)
+    g_ = torch.Generator(device=dev).manual_seed(21)
+    proj = torch.randn(T, 2 * hk * K + 2 * hv * K + 2 * hv, generator=g_, device=dev).to(torch.bfloat16)
+    q = proj[:, :hk * K].view(T, hk, K)
+    k = proj[:, hk * K:2 * hk * K].view(T, hk, K)
+    v = proj[:, 2 * hk * K:2 * hk * K + hv * K].view(T, hv, K)
+    z = proj[:, 2 * hk * K + hv * K:2 * hk * K + 2 * hv * K].view(T, hv, K)
+    a = proj[:, -2 * hv:-hv]
+    b = proj[:, -hv:]
+    A_log = torch.empty(hv, device=dev).uniform_(0, np.log(16), generator=g_)
+    dt_bias = 0.1 * torch.randn(hv, generator=g_, device=dev)
+    n_slots = len(lens) + 3
+    st0 = 0.1 * torch.randn(n_slots, hv, K, K, generator=g_, device=dev)
+    idx = torch.randperm(n_slots, generator=torch.Generator().manual_seed(4))[:len(lens)].to(torch.int32).to(dev)
+    cu = W.cu_from_lengths(lens, dev)
+    norm = RMSNormGated((K,), 1e-6).to(dev, torch.bfloat16)
+    norm.weight.data.copy_(1 + 0.1 * torch.randn(K, generator=g_, device=dev))
+    s1, s2 = st0.clone(), st0.clone()
+    out = gated_deltanet_prefill(q, k, v, a, b, A_log, dt_bias, s1, idx, cu, z, norm.weight, 1e-6)
+    o = chunk_gated_delta_rule(q, k, v, None, None, s2, idx, cu, use_qk_l2norm_in_kernel=True,
+                               gate_inputs=(a, b, A_log, dt_bias))
+    ref = norm(o, z)
+    torch.cuda.synchronize()
+    assert torch.equal(s1, s2), "final states differ between the fused and the unfused prefill"
+    assert_close(out, ref, what="fused prefill output")
