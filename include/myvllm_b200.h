@@ -29,6 +29,8 @@
  *   mvb_rmsnorm_rope            m/layers/full_attention.py:49-64      q_norm/k_norm + rotary
  *   mvb_allreduce_oneshot       m/layers/linear.py:159-164            the dist.all_reduce of
  *                                                                     RowParallelLinear.forward
+ *   mvb_linear_allreduce        m/layers/linear.py:159-164            F.linear + dist.all_reduce of
+ *                                                                     RowParallelLinear.forward, fused
  *
  * Conventions kept from the reference:
  *   - index tensors (cu_seqlens, *_indices, block_tables, context_lens, slot_mapping) are int32;
@@ -289,6 +291,22 @@ int mvb_ipc_close(void* dev_ptr);
  * at most the buffer's slot size).  out may not alias inp. */
 int mvb_allreduce_oneshot(const mvb_allreduce_peers* peers, const mvb_tensor* inp, mvb_tensor* out,
                           void* stream);
+
+/* Row-parallel projection fused with its all-reduce, one kernel per rank:
+ * out = sum over ranks r of x_r w_r^T, the output projection of a tensor-parallel layer and
+ * the dist.all_reduce after it (RowParallelLinear.forward, m/layers/linear.py:159-164).
+ * x [M, K] (this rank's input shard), w [N, K] (this rank's weight shard), out [M, N]; 16-bit,
+ * contiguous 16-byte aligned rows; M <= 128, N = 64 d with d dividing 128, K a multiple of
+ * 64 (128 / d).  The GEMM runs on the tensor cores (tcgen05, TMA-fed from this GPU's memory);
+ * the ranks' fp32 partial tiles are summed through peer loads in a fixed order, so every
+ * rank gets the same bits.  Buffers: mvb_ipc_alloc(mvb_linear_allreduce_buffer_bytes()) per
+ * rank, shared as for mvb_allreduce_oneshot; every rank calls with the same shapes in the
+ * same order.  All 128 CTAs of a launch must be resident together (no concurrent kernel
+ * may hold the GPU's SMs).  A wait for a peer that gives up sets the device error word and
+ * leaves zeros in that CTA's rows.  No multicast. */
+size_t mvb_linear_allreduce_buffer_bytes(void);
+int mvb_linear_allreduce(const mvb_allreduce_peers* peers, const mvb_tensor* x, const mvb_tensor* w, mvb_tensor* out,
+                         void* stream);
 
 /* Tensor-core self-test: D[128, n] = A B1 + (negate ? -1 : 1) A B2 on one CTA with
  * fp16 operands staged in the 128-byte-swizzle K-major (a_mn/b_mn = 0) or MN-major (= 1)

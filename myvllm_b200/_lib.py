@@ -87,6 +87,8 @@ SIGNATURES = {
     "mvb_ipc_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "mvb_ipc_close": (ctypes.c_int, [_P]),
     "mvb_allreduce_oneshot": (ctypes.c_int, [ctypes.POINTER(MvbAllReducePeers), _T, _T, _P]),
+    "mvb_linear_allreduce_buffer_bytes": (ctypes.c_size_t, []),
+    "mvb_linear_allreduce": (ctypes.c_int, [ctypes.POINTER(MvbAllReducePeers), _T, _T, _T, _P]),
     "mvb_selftest_umma": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          ctypes.c_int, _P]),
 }

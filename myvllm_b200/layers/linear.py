@@ -169,6 +169,11 @@ class RowParallelLinear(Linear):
         super().__init__(input_size // self.tp_size, output_size, bias, prefix)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.tp_size > 1 and self.bias is None:
+            # projection + all-reduce in one kernel over NVLink, where enabled and x qualifies
+            fused = comm.fused_linear(x, self.weight)
+            if fused is not None:
+                return fused
         # the bias is added once (by rank 0's share) so the all-reduced sum carries it once
         bias = self.bias if (self.bias is None or self.tp_rank == 0) else None
         result = F.linear(x, self.weight, bias)

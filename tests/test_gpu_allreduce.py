@@ -135,3 +135,113 @@ def test_oneshot_allreduce_matches_nccl():
         if p.is_alive():
             p.kill()
     assert all(results.get(r) == "ok" for r in range(N_GPUS)), dict(results)
+
+
+def _worker_fused(rank, world, port, results):
+    import datetime
+
+    import torch.distributed as dist
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        from myvllm_b200 import _lib
+        from myvllm_b200.layers import comm
+
+        f = comm.enable_fused_linear()
+        g = torch.Generator(device=dev).manual_seed(200 + rank)
+        K, N = 4096 // world, 2048
+
+        def reference(x, w):
+            xs = [torch.empty_like(x) for _ in range(world)]
+            ws = [torch.empty_like(w) for _ in range(world)]
+            dist.all_gather(xs, x)
+            dist.all_gather(ws, w)
+            return sum(a.float() @ b.float().T for a, b in zip(xs, ws))
+
+        def same_on_all_ranks(y):
+            peer = y.clone()
+            dist.broadcast(peer, 0)
+            return torch.equal(y.view(torch.int16), peer.view(torch.int16))
+
+        def close(y, ref):
+            return bool(((y.float() - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all().item())
+
+        w = (0.02 * torch.randn(N, K, generator=g, device=dev)).to(torch.bfloat16)
+        # row counts: a full decode batch, ragged, one row
+        for m in (128, 37, 1):
+            x = torch.randn(m, K, generator=g, device=dev).to(torch.bfloat16)
+            assert f.eligible(x, w)
+            y = comm.fused_linear(x, w)
+            torch.cuda.synchronize()
+            assert close(y, reference(x, w)), ("fused linear", m)
+            assert same_on_all_ranks(y), ("bits differ across ranks", m)
+        # back-to-back calls of changing row counts with no synchronisation between them, the
+        # ranks drifting apart
+        ms = [128, 5, 64, 128, 1, 100]
+        ins, outs = [], []
+        for i, m in enumerate(ms):
+            if i % world == rank:
+                torch.cuda._sleep(2_000_000)
+            x = torch.randn(m, K, generator=g, device=dev).to(torch.bfloat16)
+            ins.append(x)
+            outs.append(comm.fused_linear(x, w))
+        torch.cuda.synchronize()
+        for i, (x, y) in enumerate(zip(ins, outs)):
+            assert close(y, reference(x, w)), ("unsynchronised fused linear", i)
+        # CUDA graph replay
+        x = torch.randn(128, K, generator=g, device=dev).to(torch.bfloat16)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            comm.fused_linear(x, w)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = comm.fused_linear(x, w)
+        for it in range(3):
+            x.copy_(torch.randn(128, K, generator=g, device=dev).to(torch.bfloat16))
+            graph.replay()
+            torch.cuda.synchronize()
+            assert close(out, reference(x, w)), ("graph replay", it)
+        del graph
+        # the layer: RowParallelLinear takes the fused path and matches F.linear + NCCL
+        from myvllm_b200.layers.linear import RowParallelLinear
+
+        lin = RowParallelLinear(K * world, N, bias=False).to(dev, torch.bfloat16)
+        lin.weight.data.copy_(w)
+        x = torch.randn(16, K, generator=g, device=dev).to(torch.bfloat16)
+        y = lin(x)
+        ref = torch.nn.functional.linear(x, w)
+        dist.all_reduce(ref)
+        assert close(y, ref.float()), "RowParallelLinear fused path"
+        assert _lib.device_status() == 0
+        comm.disable_fused_linear()
+        dist.barrier()
+        dist.destroy_process_group()
+        results[rank] = "ok"
+    except Exception as e:  # noqa: BLE001
+        results[rank] = f"{type(e).__name__}: {e}"
+
+
+@needs_two
+def test_fused_linear_allreduce():
+    """mvb_linear_allreduce: each rank's x W^T (tcgen05 GEMM) and the sum over ranks in one
+    kernel, against the fp32 sum of the all-gathered partial products (bf16 bar), identical
+    bits on every rank, unsynchronised back-to-back calls, graph replay, and the
+    RowParallelLinear path."""
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_fused, args=(r, N_GPUS, port, results)) for r in range(N_GPUS)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(results.get(r) == "ok" for r in range(N_GPUS)), dict(results)
