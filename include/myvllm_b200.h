@@ -301,7 +301,8 @@ int mvb_allreduce_oneshot(const mvb_allreduce_peers* peers, const mvb_tensor* in
  * the ranks' fp32 partial tiles are summed through peer loads in a fixed order, so every
  * rank gets the same bits.  Buffers: mvb_ipc_alloc(mvb_linear_allreduce_buffer_bytes()) per
  * rank, shared as for mvb_allreduce_oneshot; every rank calls with the same shapes in the
- * same order.  All 128 CTAs of a launch must be resident together (no concurrent kernel
+ * same order (world 1 is allowed: the same kernel as a single-rank projection).  All 128
+ * CTAs of a launch must be resident together (no concurrent kernel
  * may hold the GPU's SMs).  A wait for a peer that gives up sets the device error word and
  * leaves zeros in that CTA's rows.  No multicast. */
 size_t mvb_linear_allreduce_buffer_bytes(void);

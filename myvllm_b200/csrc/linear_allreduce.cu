@@ -223,8 +223,8 @@ extern "C" int mvb_linear_allreduce(const mvb_allreduce_peers* peers, const mvb_
   using namespace mvb;
   const char* op = "linear_allreduce";
   MVB_CHECK_ARG(peers != nullptr && x != nullptr && w != nullptr && out != nullptr, "%s: NULL argument", op);
-  MVB_CHECK_ARG(peers->world >= 2 && peers->world <= kMaxRanks && peers->rank >= 0 && peers->rank < peers->world,
-                "%s: world %d / rank %d out of range (2..%d ranks)", op, peers->world, peers->rank, kMaxRanks);
+  MVB_CHECK_ARG(peers->world >= 1 && peers->world <= kMaxRanks && peers->rank >= 0 && peers->rank < peers->world,
+                "%s: world %d / rank %d out of range (1..%d ranks)", op, peers->world, peers->rank, kMaxRanks);
   MVB_CHECK_ARG(peers->buf_bytes >= kDataOff + 2 * kSlotBytes, "%s: buffers smaller than %zu bytes", op,
                 (size_t)(kDataOff + 2 * kSlotBytes));
   for (int r = 0; r < peers->world; ++r)

@@ -245,3 +245,31 @@ def test_fused_linear_allreduce():
         if p.is_alive():
             p.kill()
     assert all(results.get(r) == "ok" for r in range(N_GPUS)), dict(results)
+
+
+def test_fused_linear_single_rank():
+    """mvb_linear_allreduce with one rank (the kernel's GEMM tiles, the split-K partials in its
+    buffer and their reduction, without peers) against torch fp32 x W^T, on one GPU; two calls
+    in a row exercise the slot alternation."""
+    import ctypes
+
+    from myvllm_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    lib = _lib.load()
+    buf = torch.zeros(int(lib.mvb_linear_allreduce_buffer_bytes()) + 256, dtype=torch.uint8, device=dev)
+    base = (buf.data_ptr() + 255) // 256 * 256
+    peers = _lib.MvbAllReducePeers()
+    peers.world, peers.rank, peers.buf_bytes = 1, 0, int(lib.mvb_linear_allreduce_buffer_bytes())
+    peers.bufs[0] = base
+    g = torch.Generator(device=dev).manual_seed(7)
+    for m, k, n in ((128, 4096, 2048), (37, 1024, 2048), (1, 512, 4096)):
+        x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+        w = (0.02 * torch.randn(n, k, generator=g, device=dev)).to(torch.bfloat16)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        _lib.call("linear_allreduce", "mvb_linear_allreduce", ctypes.byref(peers), _lib.desc(x), _lib.desc(w),
+                  _lib.desc(out), _lib.stream_of(x))
+        ref = x.float() @ w.float().T
+        torch.cuda.synchronize()
+        assert bool(((out.float() - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all().item()), (m, k, n)
+    assert _lib.device_status() == 0
