@@ -715,13 +715,16 @@ def run_c4(args, rank, world, device):
     from myvllm_b200.decode_stack import HybridDecodeStack, hidden_input
 
     S, n_layers = args.seqs or 128, args.layers or 48
-    oneshot = None
-    if world > 1 and args.allreduce == "oneshot":
+    oneshot = fused = None
+    if world > 1 and args.allreduce in ("oneshot", "fused"):
         from myvllm_b200.layers import comm
 
         # the o_proj / out_proj partial sums ([128, 2048] bf16, 512 KiB) go through the
-        # one-shot NVLink kernel instead of NCCL
+        # one-shot NVLink kernel instead of NCCL; with "fused" the projection and its
+        # all-reduce run as one kernel (decode batches), the one-shot kernel covering the rest
         oneshot = comm.enable_oneshot(max_bytes=2 << 20)
+        if args.allreduce == "fused":
+            fused = comm.enable_fused_linear()
     ctx_lens = W.seq_lengths(S, 1024, 32768, 4)
     n_max = max(args.steps, 300)
     stack = HybridDecodeStack(n_layers, S, ctx_lens, args.warmup + n_max + 8, device, seed=1234)
@@ -782,6 +785,8 @@ def run_c4(args, rank, world, device):
         from myvllm_b200.layers import comm
 
         comm.disable_oneshot()  # raises if a one-shot wait gave up
+        if fused is not None:
+            comm.disable_fused_linear()
     by = stack.bytes_per_step()
     del stack
     torch.cuda.empty_cache()
@@ -799,6 +804,8 @@ def run_c4(args, rank, world, device):
                                     f"hidden 2048, {S} seqs, ctx ~U[1024,32768]",
                         "parallelism": f"tp{world}", "l2": "KV and states far larger than L2",
                         "all_reduce": ("none" if world == 1 else
+                                       "output projection + all-reduce in one kernel (mvb_linear_allreduce)"
+                                       if fused is not None else
                                        "one-shot NVLink kernel (mvb_allreduce_oneshot)" if oneshot is not None
                                        else "NCCL"),
                         "execution": "one CUDA graph per decode step"},
@@ -898,8 +905,9 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="c4: layers instead of 48 (a multiple of 4; smaller cases for profiler captures)")
     ap.add_argument("--seqs", type=int, default=None, help="c4: sequences instead of 128 (profiler cases)")
-    ap.add_argument("--allreduce", default="oneshot", choices=["oneshot", "nccl"],
-                    help="c4 at N > 1: the tensor-parallel all-reduce after each output projection")
+    ap.add_argument("--allreduce", default="oneshot", choices=["oneshot", "fused", "nccl"],
+                    help="c4 at N > 1: the tensor-parallel all-reduce after each output projection (fused: the "
+                         "projection and its all-reduce in one kernel)")
     ap.add_argument("--lengths", default=None,
                     help="c1/c3: sequence lengths instead of the config's seeded draw, e.g. 8x2048 or 700,1500 "
                          "(smaller cases for profiler captures)")

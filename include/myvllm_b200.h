@@ -140,12 +140,19 @@ int mvb_fused_recurrent_gdn_gated(const mvb_tensor* q, const mvb_tensor* k, cons
  * [S_max, W-1, conv_dim] and recurrent_state [S_max, Hv, K, V] (fp32), both updated in
  * place at conv_state_indices / recurrent_state_indices; a, b [S, Hv] raw gate projections;
  * A_log, dt_bias [Hv]; z [S, Hv, V] the norm's gate; norm_weight [V]; out [S, Hv, V] =
- * RMSNormGated(o, z).  K = V = 128 and Hv / Hk in {1, 2, 4}; scale <= 0 means K^-0.5. */
+ * RMSNormGated(o, z).  K = V = 128; scale <= 0 means K^-0.5.
+ * counters / records: caller memory of at least the sizes mvb_gated_deltanet_decode_workspace_sizes
+ * reports.  counters must be zero before the first call and are left at zero by every call
+ * (keep them apart from any other use); records need no initial value (16-byte aligned).
+ * Launches that share them must be ordered (same stream). */
+int mvb_gated_deltanet_decode_workspace_sizes(int64_t n_seqs, int64_t num_k_heads, int64_t num_v_heads,
+                                              size_t* counters_bytes, size_t* records_bytes);
 int mvb_gated_deltanet_decode(const mvb_tensor* qkv, const mvb_tensor* conv_weight, mvb_tensor* conv_state,
                               const mvb_tensor* conv_state_indices, const mvb_tensor* a, const mvb_tensor* b,
                               const mvb_tensor* a_log, const mvb_tensor* dt_bias, mvb_tensor* recurrent_state,
                               const mvb_tensor* recurrent_state_indices, const mvb_tensor* z,
                               const mvb_tensor* norm_weight, float norm_eps, float scale, mvb_tensor* out,
+                              void* counters, size_t counters_bytes, void* records, size_t records_bytes,
                               void* stream);
 
 /* The prefill branch of a Gated DeltaNet layer after its conv: mvb_chunk_gated_delta_rule_gated

@@ -62,7 +62,10 @@ SIGNATURES = {
     "mvb_chunk_gated_delta_rule_gated": (ctypes.c_int, [_T] * 11 + [ctypes.c_float, ctypes.c_int, _P, ctypes.c_size_t,
                                                                     _P]),
     "mvb_fused_recurrent_gdn_gated": (ctypes.c_int, [_T] * 10 + [ctypes.c_float, ctypes.c_int, _P]),
-    "mvb_gated_deltanet_decode": (ctypes.c_int, [_T] * 12 + [ctypes.c_float, ctypes.c_float, _T, _P]),
+    "mvb_gated_deltanet_decode_workspace_sizes": (ctypes.c_int, [ctypes.c_int64] * 3 +
+                                                  [ctypes.POINTER(ctypes.c_size_t)] * 2),
+    "mvb_gated_deltanet_decode": (ctypes.c_int, [_T] * 12 + [ctypes.c_float, ctypes.c_float, _T, _P, ctypes.c_size_t,
+                                                             _P, ctypes.c_size_t, _P]),
     "mvb_gated_deltanet_prefill": (ctypes.c_int, [_T] * 12 + [ctypes.c_float, _T, ctypes.c_float, _P, ctypes.c_size_t,
                                                               _P]),
     "mvb_flash_attention_prefill": (ctypes.c_int, [_T, _T, _T, _T, ctypes.c_float, ctypes.c_int, ctypes.c_int,

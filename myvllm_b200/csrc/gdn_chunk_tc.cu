@@ -23,13 +23,13 @@
 // accumulators fp32 (the final fp32 state stays within 1e-3 relative of the exact recurrence).
 //
 // Two warp groups pipeline consecutive chunks:
-//   prep (warps 0-7): TMA loads, gates, D1, the mask of A, triangular solve and the U/W
-//                     factors for chunk c+1 -- nothing here depends on the state;
-//   rec  (warps 8-11, thread = TMEM lane): q'/k', Aqk, the U/W products and the W staging,
-//                     then Vn, O and the state update for chunk c, the output tile and the
-//                     fp16 state copy for chunk c+1.
+//   prep (warps 0-7): TMA loads, gates, D1, masks, triangular solve and the U/W factors for
+//                     chunk c+1 -- nothing here depends on the state;
+//   rec  (warps 8-11, thread = TMEM lane): q'/k', the U/W products and the W staging, then
+//                     Vn, O and the state update for chunk c, the output tile and the fp16
+//                     state copy for chunk c+1.
 // They hand buffers over through mbarriers (normed / factors-ready / gates-ready from prep;
-// MMA completions and D1-read from rec).  prep publishes chunk c+1 only once the U/W products of chunk
+// MMA completions from rec).  prep publishes chunk c+1 only once the U/W products of chunk
 // c are done, which keeps it at most one phase ahead on every barrier.  Chains are handed out longest sequence first over a
 // persistent grid: dynamically through a work counter when the caller supplies one (the
 // last CTA to run dry zeroes it for the next launch), else round-robin.  Every wait is
@@ -94,7 +94,7 @@ struct Params {
 };
 
 struct Bars {
-  uint64_t raw_qk[2], raw_v, d1_done, mma2_done, mma_r, gready[2], r4done, aqk_done;
+  uint64_t raw_qk[2], raw_v, d1_done, mma2_done, mma_r, gready[2], r4done;
   uint64_t mma2_go, normed, mma_all, mma_all_prep;
 };
 
@@ -290,7 +290,7 @@ struct Item {
   bool valid, first;
 };
 
-template <typename T>
+template <typename T, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) char smem_raw[];
   char* sm = umma::align1024(smem_raw);
@@ -337,7 +337,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     umma::mbar_init(&bars.mma2_done, 1);
     umma::mbar_init(&bars.mma_r, 1);
     umma::mbar_init(&bars.r4done, 1);
-    umma::mbar_init(&bars.aqk_done, 1);
     umma::mbar_fence_init();
   }
   if (warp == 0) umma::tmem_alloc(&tmem_slot, TMEM_COLS);
@@ -467,13 +466,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       }
     };
     // raw tile of chunk kk landed -> D1 = [q; k] k^T on the tensor core (the D1 tile of chunk
-    // kk-1 has been read: its mask precedes this call, its Aqk is awaited below) -> q/k norms
-    // (and G - log2(1/|k|) per k column)
+    // kk-1 has been read: its mask and Aqk precede this call) -> q/k norms (and
+    // G - log2(1/|k|) per k column)
     auto norms = [&](int kk) -> bool {
       bool w = umma::mbar_wait(&bars.raw_qk[kk & 1], (kk >> 1) & 1);
       if (tid == 0) qk_used = kk + 1;
-      // rec has read D1 of chunk kk-1 (its Aqk) before this chunk's D1 overwrites it
-      if (tid == 0 && kk >= 1) w = w && umma::mbar_wait(&bars.aqk_done, (kk - 1) & 1);
       if (!(w = bar_and(kBarPrep, kPrep, w))) return false;
       const char* qk = sm + SM_QK + (kk & 1) * 32768;
       if (tid == 0) {
@@ -605,9 +602,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       // ---- Ti = (I + A)^-1 ----
       solve_tril64(sm + SM_A, sm + SM_A + 8192, reinterpret_cast<const float*>(sm + SM_AD), sm + SM_T,
                    sm + SM_T + 8192, tid);
+      if (tid == 0 && k >= 1) ok = umma::mbar_wait(&bars.r4done, (k - 1) & 1);  // Aqk buffer free
+      if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
 
       // ---- U/W factors split hi + lo in the input type (they overwrite Ti: read all, then
-      //      write) ----
+      //      write); Aqk (fp16) from the q rows of D1 ----
       {
         uint4 fo[2][4];
 #pragma unroll
@@ -641,6 +640,29 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
           for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(sm + SM_TF + q * 8192 + off) = fo[it][q];
         }
       }
+      if (tl < 64) {
+        float v[32];
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
+        const int i = tl;
+        const float rowf = p.scale * sFk[F_QN + i];
+        const float gi = sFk[F_G + i];
+        float gc[32];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const float4 x = *reinterpret_cast<const float4*>(sFk + F_GC + wg * 32 + 4 * m);
+          gc[4 * m] = x.x; gc[4 * m + 1] = x.y; gc[4 * m + 2] = x.z; gc[4 * m + 3] = x.w;
+        }
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float e = ex2(gi - gc[j]);
+          v[j] = wg * 32 + j <= i ? rowf * v[j] * e : 0.f;
+        }
+#pragma unroll
+        for (int cch = 0; cch < 4; ++cch)
+          *reinterpret_cast<uint4*>(sm + SM_AQK + umma::sw128(i, wg * 4 + cch)) = pack8<__half>(v + cch * 8);
+      }
       umma::fence_async_smem();
       umma::fence_before();
       bar_sync(kBarPrep, kPrep);
@@ -649,10 +671,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       if (tid == 0) tma::arrive(&bars.mma2_go);
 
       // ---- meanwhile: gates and norms of chunk k+1 (once rec has read chunk k's) ----
-      // (gates(k+1) rewrites the gate slot of chunk k-1, which rec reads until it issues the
-      // output/state MMAs of that chunk)
-      if (tid == 0 && k >= 1) ok = umma::mbar_wait(&bars.r4done, (k - 1) & 1);
-      if (!(ok = bar_and(kBarPrep, kPrep, ok))) break;
       Item nxt2 = nxt;
       if (nxt.valid) {
         nxt2 = next_item(nxt);
@@ -705,22 +723,43 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     const uint32_t id_s = umma::idesc_f16(128, 128, true, false);
     // deferred store of the last output tile (o tile in SM_O; pend_n == 0: nothing pending)
     int pend_c0 = 0, pend_h = 0, pend_n = 0;
-    // The 16 lanes of a half warp store one token row (16 x 8 columns); with the layer's
-    // output norm they first form its RMS over the 128 columns by a 4-step shuffle and apply
-    // RMSNormGated to the rounded tile, as the reference applies it to the op's output.
-    const bool norm = p.nd.z != nullptr;
-    float nw8[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) nw8[j] = norm ? load_scalar(p.nd.w, (rt & 15) * 8 + j, p.nd.w_dt) : 1.f;
+    // Without the layer's output norm: a plain copy of the tile.  With it, the 16 lanes of a
+    // half warp that store one token row (16 x 8 columns) first form the row's RMS over the 128
+    // columns by a 4-step shuffle and apply RMSNormGated to the rounded tile, as the reference
+    // applies it to the op's output.
     auto store_o = [&]() {
-      for (int e = rt; e < C * 16; e += kRec) {
-        const int i = e >> 4, c16 = e & 15;
-        const bool live = i < pend_n;
-        uint4 val = live ? *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7))
-                         : make_uint4(0, 0, 0, 0);
-        if (norm) {  // uniform: every lane takes part in the shuffles
+      if constexpr (!NORM) {
+        for (int e = rt; e < C * 16; e += kRec) {
+          const int i = e >> 4, c16 = e & 15;
+          if (i < pend_n) {
+            const uint4 val = *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7));
+            *reinterpret_cast<uint4*>(go + (int64_t)(pend_c0 + i) * p.so_t + (int64_t)pend_h * p.so_h + c16 * 8) = val;
+          }
+        }
+      } else {
+        // this thread's columns are fixed (c16 = rt & 15): their norm weights, then the z rows
+        // of all its tokens in flight at once, then the rows
+        const int c16 = rt & 15;
+        float nw8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) nw8[j] = load_scalar(p.nd.w, c16 * 8 + j, p.nd.w_dt);
+        uint4 zr[C * 16 / kRec];
+#pragma unroll
+        for (int it = 0; it < C * 16 / kRec; ++it) {
+          const int i = (rt + it * kRec) >> 4;
+          zr[it] = i < pend_n ? *reinterpret_cast<const uint4*>(static_cast<const T*>(p.nd.z) +
+                                                                 (int64_t)(pend_c0 + i) * p.nd.z_t +
+                                                                 (int64_t)pend_h * p.nd.z_h + c16 * 8)
+                              : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int it = 0; it < C * 16 / kRec; ++it) {  // uniform trip count: every lane shuffles
+          const int i = (rt + it * kRec) >> 4;
+          const bool live = i < pend_n;
           float f[8], zf[8];
-          unpack8<T>(val, f);
+          unpack8<T>(live ? *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7))
+                          : make_uint4(0, 0, 0, 0),
+                     f);
           float ss = 0.f;
 #pragma unroll
           for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
@@ -728,15 +767,19 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
           for (int off = 1; off < 16; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
           if (live) {
             const float r = rsqrtf(ss / (float)D + p.nd.eps);
-            unpack8<T>(*reinterpret_cast<const uint4*>(static_cast<const T*>(p.nd.z) + (int64_t)(pend_c0 + i) * p.nd.z_t +
-                                                       (int64_t)pend_h * p.nd.z_h + c16 * 8),
-                       zf);
+            unpack8<T>(zr[it], zf);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) f[j] = f[j] * r * nw8[j] * silu(zf[j]);
-            val = pack8<T>(f);
+            for (int j = 0; j < 8; ++j) {
+              // silu(z) = z sigmoid(z) = 0.5 z (1 + tanh(z / 2)): one MUFU op
+              const float hz = 0.5f * zf[j];
+              float th;
+              asm("tanh.approx.f32 %0, %1;" : "=f"(th) : "f"(hz));
+              f[j] = f[j] * r * nw8[j] * fmaf(hz, th, hz);
+            }
+            *reinterpret_cast<uint4*>(go + (int64_t)(pend_c0 + i) * p.so_t + (int64_t)pend_h * p.so_h + c16 * 8) =
+                pack8<T>(f);
           }
         }
-        if (live) *reinterpret_cast<uint4*>(go + (int64_t)(pend_c0 + i) * p.so_t + (int64_t)pend_h * p.so_h + c16 * 8) = val;
       }
       pend_n = 0;
     };
@@ -773,35 +816,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
             *reinterpret_cast<uint4*>(dst + hh * 8192 + umma::sw128(i, c)) = pack8<__half>(f);
           }
       }
-      // ---- Aqk = lower(scale D1[q] e^{G_i - G_j} / |q_i||k_j|) (fp16) from the q rows of D1
-      //      (TMEM lanes 0-63: warps 8 and 9, one row each, all 64 columns) ----
-      if (rt < 64) {
-        const float* sFk = sF + b * kFSet;
-        float v[64];
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + q4 * 16), v + q4 * 16);
-        const int i = rt;
-        const float rowf = p.scale * sFk[F_QN + i];
-        const float gi = sFk[F_G + i];
-        umma::tmem_wait_ld();
-#pragma unroll
-        for (int q4 = 0; q4 < 16; ++q4) {
-          const float4 x = *reinterpret_cast<const float4*>(sFk + F_GC + 4 * q4);
-          const float gc[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int col = q4 * 4 + j;
-            v[col] = col <= i ? rowf * v[col] * ex2(gi - gc[j]) : 0.f;
-          }
-        }
-#pragma unroll
-        for (int cch = 0; cch < 8; ++cch)
-          *reinterpret_cast<uint4*>(sm + SM_AQK + umma::sw128(i, cch)) = pack8<__half>(v + cch * 8);
-      }
       umma::fence_async_smem();
-      umma::fence_before();
       bar_sync(kBarRec, kRec);
-      if (rt == 0) tma::arrive(&bars.aqk_done);
 
       // ---- U^T = v^T (Tu_hi + Tu_lo)^T, W^T = k^T (Tw_hi + Tw_lo)^T once prep has the factors ----
       if (rt == 0) {
@@ -971,6 +987,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       pend_c0 = rec.c0;
       pend_h = rec.h;
       pend_n = rec.n;
+      if constexpr (NORM) {  // the z rows of this tile into L2 now, for the store a chunk later
+        if (rt < pend_n)
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], 256;" ::"l"(static_cast<const T*>(p.nd.z) +
+                                                                         (int64_t)(pend_c0 + rt) * p.nd.z_t +
+                                                                         (int64_t)pend_h * p.nd.z_h)
+                       : "memory");
+      }
     }
     if (ok) store_o();
     if (rt == 0) {
@@ -1035,14 +1058,27 @@ int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* 
   p.nd = nd;
   const int chains = (int)(n_seqs * p.hv);
   const int grid = chains < num_sms() ? chains : num_sms();
+  const bool norm = nd.z != nullptr;
   if (q->dtype == MVB_BF16) {
-    static unsigned long long attr_mask = 0;
-    ensure_smem_attr(gdn_chunk_tc_kernel<__nv_bfloat16>, SMEM_BYTES, attr_mask);
-    gdn_chunk_tc_kernel<__nv_bfloat16><<<grid, kThreads, SMEM_BYTES, st>>>(p);
+    if (norm) {
+      static unsigned long long attr_mask = 0;
+      ensure_smem_attr(gdn_chunk_tc_kernel<__nv_bfloat16, true>, SMEM_BYTES, attr_mask);
+      gdn_chunk_tc_kernel<__nv_bfloat16, true><<<grid, kThreads, SMEM_BYTES, st>>>(p);
+    } else {
+      static unsigned long long attr_mask = 0;
+      ensure_smem_attr(gdn_chunk_tc_kernel<__nv_bfloat16, false>, SMEM_BYTES, attr_mask);
+      gdn_chunk_tc_kernel<__nv_bfloat16, false><<<grid, kThreads, SMEM_BYTES, st>>>(p);
+    }
   } else {
-    static unsigned long long attr_mask = 0;
-    ensure_smem_attr(gdn_chunk_tc_kernel<__half>, SMEM_BYTES, attr_mask);
-    gdn_chunk_tc_kernel<__half><<<grid, kThreads, SMEM_BYTES, st>>>(p);
+    if (norm) {
+      static unsigned long long attr_mask = 0;
+      ensure_smem_attr(gdn_chunk_tc_kernel<__half, true>, SMEM_BYTES, attr_mask);
+      gdn_chunk_tc_kernel<__half, true><<<grid, kThreads, SMEM_BYTES, st>>>(p);
+    } else {
+      static unsigned long long attr_mask = 0;
+      ensure_smem_attr(gdn_chunk_tc_kernel<__half, false>, SMEM_BYTES, attr_mask);
+      gdn_chunk_tc_kernel<__half, false><<<grid, kThreads, SMEM_BYTES, st>>>(p);
+    }
   }
   MVB_CHECK_LAUNCH("chunk_gated_delta_rule");
   return MVB_OK;

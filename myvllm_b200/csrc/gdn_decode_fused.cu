@@ -9,17 +9,19 @@
 // kernel reads the projection row, the conv and recurrent states and z once, and writes
 // the states and the normed output once.
 //
-// Grid (2, Hv, S): a CTA owns one half (64 columns) of the V axis of one (sequence, v-head),
-// with the state streamed through registers exactly as gdn_recurrent.cu does it.  CTAs are
-// grouped in clusters of (2, G) = both V halves of the G = Hv / Hk v-heads that share one
-// k-head:
+// Grid (2, Hv, S), 128 threads: a CTA owns one half (64 columns) of the V axis of one
+// (sequence, v-head), with the state streamed through registers exactly as
+// gdn_recurrent.cu does it (four such CTAs fit an SM).  Work shared between CTAs is handed
+// to whichever CTA finishes its part last, through counters in caller memory (zero-initialised
+// once; every counter returns to zero), so no CTA waits for another:
 //   - every CTA recomputes the conv of its k-head's q and k channels (256 channels, 4 taps:
-//     cheaper than exchanging them), and of its own 64 v channels;
-//   - the v channels' conv state is written by the CTA that owns them; the q/k channels'
-//     state, read by all 2G CTAs, is written by the cluster's first CTA after a cluster
-//     barrier that follows every CTA's read;
-//   - the RMS over the 128 V columns adds the two halves' partial sums through distributed
-//     shared memory (in a fixed order, so both halves use the same bits).
+//     cheaper than exchanging them) and of its own 64 v channels, and shifts the conv state
+//     of those v channels, which no other CTA reads;
+//   - the q/k channels' conv state is read by the 2 G CTAs of the G = Hv / Hk v-heads that
+//     share the k-head: each counts itself out after its read, and the last one shifts it;
+//   - each half writes its 64 (rounded) o values and their sum of squares to the workspace
+//     and counts itself out; the last of the two forms the RMS over all 128 columns (the
+//     halves' sums added in half order) and writes both halves' normed output.
 // Numerics follow the unfused ops: the conv output is rounded to the activation dtype
 // before the norms, o is rounded before RMSNormGated, all arithmetic is fp32.
 #include "common.cuh"
@@ -28,10 +30,11 @@ namespace mvb {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int K = 128, VS = 64;  // head dims (K = V = 128); V columns per CTA
-constexpr int CG = VS / 4;       // float4 column groups per CTA
+constexpr int K = 128, VS = 64;    // head dims (K = V = 128); V columns per CTA
+constexpr int CG = VS / 4;         // float4 column groups per CTA
 constexpr int RP = kThreads / CG;  // state rows per pass
 constexpr int NI = K / RP;         // passes over K
+constexpr int kHalfFloats = VS + 4;  // per (sequence, head, half): 64 o values, their sum of squares, pad
 
 struct FusedParams {
   const void* qkv;  // [S, conv_dim] projection rows (q | k | v channels)
@@ -54,26 +57,12 @@ struct FusedParams {
   int nw_dt;
   void* out;  // [S, Hv, V] (strides o_t, o_h)
   int64_t o_t, o_h;
+  int* cnt_conv;  // [S, Hk]  CTAs done reading the shared q/k conv state
+  int* cnt_norm;  // [S, Hv]  halves done with their o
+  float* half_o;  // [S, Hv, 2, kHalfFloats]
   int hk, hv, group;
   float scale, eps;
 };
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// A float in the shared memory of CTA `rank` of this cluster.
-__device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
-  uint32_t local = smem_u32(p), remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
-}
 
 // x sigmoid(x) through tanh.approx, as the conv kernels compute it.
 __device__ __forceinline__ float silu_conv(float x) {
@@ -83,19 +72,27 @@ __device__ __forceinline__ float silu_conv(float x) {
   return fmaf(h, t, h);
 }
 
+// Counts this CTA out of `cnt` (its earlier memory operations made visible first); true for
+// the CTA that completes the count `total`, which also resets it for the next launch.
+__device__ __forceinline__ bool count_out(int* cnt, int total) {
+  __threadfence();
+  const bool last = atomicAdd(cnt, 1) == total - 1;
+  if (last) *cnt = 0;
+  return last;
+}
+
 template <typename T, typename TW, int W>
 __global__ void __launch_bounds__(kThreads) gdn_decode_fused_kernel(const __grid_constant__ FusedParams p) {
   __shared__ float sq[K], sk[K], sv[VS];
   __shared__ float4 red_a[kThreads / 32][32], red_b[kThreads / 32][32];
   __shared__ float red_qk[kThreads / 32][32];
   __shared__ float s_gb[2], s_nrm[2];
-  __shared__ float s_part;  // this half's sum of o^2, read by the other half
+  __shared__ int s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cg = tid % CG, rg = tid / CG;
   const int half = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
   const int kh = h / p.group;
-  const uint32_t crank = cluster_rank();
   const int vcol = half * VS + cg * 4;  // this thread's 4 state columns
 
   // ---- recurrent state loads first: the longest latency, independent of the conv ----
@@ -104,34 +101,37 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_fused_kernel(const __grid
 #pragma unroll
   for (int i = 0; i < NI; ++i) s[i] = __ldcs(reinterpret_cast<const float4*>(S + (int64_t)(rg + RP * i) * p.ss_k));
 
-  // ---- conv of this CTA's channels: q (16 x 8), k (16 x 8), own v half (8 x 8) ----
+  // ---- conv, four channels a thread: q (32 x 4), k (32 x 4), own v half (16 x 4) ----
   const int qt = p.hk * K;  // q channels; k channels follow, then v
-  int c0 = -1, job = tid;   // first channel of this thread's 8, or -1
-  if (job < 16) c0 = kh * K + job * 8;
-  else if (job < 32) c0 = qt + kh * K + (job - 16) * 8;
-  else if (job < 40) c0 = 2 * qt + h * 2 * VS + half * VS + (job - 32) * 8;
-  float xin[8], hist[W > 1 ? W - 1 : 1][8];
+  const int job = tid;
+  int c0 = -1;  // first channel of this thread's four, or -1
+  if (job < 32) c0 = kh * K + 4 * job;
+  else if (job < 64) c0 = qt + kh * K + 4 * (job - 32);
+  else if (job < 80) c0 = 2 * qt + h * 2 * VS + half * VS + 4 * (job - 64);
   T* cst = static_cast<T*>(p.cst) + (int64_t)p.cidx[seq] * p.cs_n;
+  const T* xrow = static_cast<const T*>(p.qkv) + (int64_t)seq * p.sx;
   if (c0 >= 0) {
-    unpack8<T>(*reinterpret_cast<const uint4*>(static_cast<const T*>(p.qkv) + (int64_t)seq * p.sx + c0), xin);
+    const uint2 xin = *reinterpret_cast<const uint2*>(xrow + c0);
+    uint2 hist[W - 1];
 #pragma unroll
-    for (int j = 0; j < W - 1; ++j) unpack8<T>(*reinterpret_cast<const uint4*>(cst + j * p.cs_t + c0), hist[j]);
+    for (int j = 0; j < W - 1; ++j) hist[j] = *reinterpret_cast<const uint2*>(cst + j * p.cs_t + c0);
     const TW* wt = static_cast<const TW*>(p.cw) + (int64_t)c0 * p.cw_c;
-    float acc[8];
+    float acc[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
       float a = 0.f;
 #pragma unroll
-      for (int j = 0; j < W; ++j) a += to_f32<TW>(wt[(int64_t)i * p.cw_c + j * p.cw_j]) * (j == W - 1 ? xin[i] : hist[j][i]);
+      for (int j = 0; j < W; ++j) {
+        const uint2 u = j == W - 1 ? xin : hist[j];
+        a += to_f32<TW>(wt[(int64_t)i * p.cw_c + j * p.cw_j]) * to_f32<T>(reinterpret_cast<const T*>(&u)[i]);
+      }
       acc[i] = to_f32<T>(from_f32<T>(silu_conv(a)));  // the activation dtype, as the conv op writes it
     }
-    float* dst = job < 16 ? sq + job * 8 : (job < 32 ? sk + (job - 16) * 8 : sv + (job - 32) * 8);
+    float* dst = job < 32 ? sq + 4 * job : (job < 64 ? sk + 4 * (job - 32) : sv + 4 * (job - 64));
+    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (job >= 64) {  // own v channels: no other CTA reads them
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dst[i] = acc[i];
-    if (job >= 32) {  // own v channels: shift this CTA's part of the conv state now
-#pragma unroll
-      for (int j = 0; j < W - 1; ++j)
-        *reinterpret_cast<uint4*>(cst + j * p.cs_t + c0) = pack8<T>(j + 1 < W - 1 ? hist[j + 1] : xin);
+      for (int j = 0; j < W - 1; ++j) *reinterpret_cast<uint2*>(cst + j * p.cs_t + c0) = j + 1 < W - 1 ? hist[j + 1] : xin;
     }
   }
   if (tid == 0) {
@@ -140,12 +140,18 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_fused_kernel(const __grid
     s_gb[0] = expf(raw_gate_g(p.gd, gv, h));
     s_gb[1] = raw_gate_beta(bv, p.b_dt);
   }
-  // every CTA of the cluster has read the shared q/k conv state -> the first one shifts it
-  cluster_sync();
-  if (crank == 0 && c0 >= 0 && job < 32) {
+  __syncthreads();
+  // this CTA has read the shared q/k conv state; the last of its 2 G readers shifts it
+  if (tid == 0) s_last = count_out(p.cnt_conv + (int64_t)seq * p.hk + kh, 2 * p.group);
+  __syncthreads();
+  if (s_last && c0 >= 0 && job < 64) {
+    __threadfence();
+    uint2 rows[W];
 #pragma unroll
-    for (int j = 0; j < W - 1; ++j)
-      *reinterpret_cast<uint4*>(cst + j * p.cs_t + c0) = pack8<T>(j + 1 < W - 1 ? hist[j + 1] : xin);
+    for (int j = 1; j < W - 1; ++j) rows[j] = __ldcg(reinterpret_cast<const uint2*>(cst + j * p.cs_t + c0));
+    rows[W - 1] = *reinterpret_cast<const uint2*>(xrow + c0);
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) *reinterpret_cast<uint2*>(cst + j * p.cs_t + c0) = rows[j + 1];
   }
 
   // ---- q/k L2 norms (x rsqrt(sum x^2 + 1e-6), m/layers/linear_attention.py:113-114) ----
@@ -218,77 +224,82 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_fused_kernel(const __grid
     s[i].x = decay * s[i].x + kr * vn.x; s[i].y = decay * s[i].y + kr * vn.y;
     s[i].z = decay * s[i].z + kr * vn.z; s[i].w = decay * s[i].w + kr * vn.w;
   }
-#pragma unroll
-  for (int i = 0; i < NI; ++i) __stcs(reinterpret_cast<float4*>(S + (int64_t)(rg + RP * i) * p.ss_k), s[i]);
 
-  // ---- o (rounded to the activation dtype, as the op returns it) and its sum of squares ----
-  float o4[4] = {0.f, 0.f, 0.f, 0.f};
-  float part = 0.f;
+  // ---- o (rounded to the activation dtype, as the op returns it) -> this half's record ----
+  float* rec = p.half_o + ((int64_t)seq * p.hv + h) * 2 * kHalfFloats;
   if (rg == 0) {  // threads 0-15 of warp 0: 4 columns each
     const float sc = p.scale;
-    o4[0] = to_f32<T>(from_f32<T>(sc * (decay * bq.x + qk * vn.x)));
-    o4[1] = to_f32<T>(from_f32<T>(sc * (decay * bq.y + qk * vn.y)));
-    o4[2] = to_f32<T>(from_f32<T>(sc * (decay * bq.z + qk * vn.z)));
-    o4[3] = to_f32<T>(from_f32<T>(sc * (decay * bq.w + qk * vn.w)));
-    part = o4[0] * o4[0] + o4[1] * o4[1] + o4[2] * o4[2] + o4[3] * o4[3];
+    const float o4[4] = {to_f32<T>(from_f32<T>(sc * (decay * bq.x + qk * vn.x))),
+                         to_f32<T>(from_f32<T>(sc * (decay * bq.y + qk * vn.y))),
+                         to_f32<T>(from_f32<T>(sc * (decay * bq.z + qk * vn.z))),
+                         to_f32<T>(from_f32<T>(sc * (decay * bq.w + qk * vn.w)))};
+    *reinterpret_cast<float4*>(rec + half * kHalfFloats + cg * 4) = make_float4(o4[0], o4[1], o4[2], o4[3]);
+    float part = o4[0] * o4[0] + o4[1] * o4[1] + o4[2] * o4[2] + o4[3] * o4[3];
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) part += __shfl_xor_sync(0x0000ffffu, part, off);
+    if (lane == 0) rec[half * kHalfFloats + VS] = part;
   }
-  if (warp == 0) {
-    part = warp_sum(part);
-    if (lane == 0) s_part = part;
-  }
-  // both halves' partial sums are written -> read the other half's; the last barrier keeps
-  // every CTA's shared memory alive until its peer has read it
-  cluster_sync();
-  const float p0 = half == 0 ? s_part : ld_dsmem(&s_part, crank ^ 1u);
-  const float p1 = half == 1 ? s_part : ld_dsmem(&s_part, crank ^ 1u);
-  cluster_sync();
-  if (rg == 0) {
-    const float r = rsqrtf((p0 + p1) / (float)(2 * VS) + p.eps);
-    const T* zr = static_cast<const T*>(p.z) + (int64_t)seq * p.z_t + (int64_t)h * p.z_h + vcol;
-    T* orow = static_cast<T*>(p.out) + (int64_t)seq * p.o_t + (int64_t)h * p.o_h + vcol;
+  __syncthreads();
+  // the last of the two halves writes the normed output of both
+  if (tid == 0) s_last = count_out(p.cnt_norm + (int64_t)seq * p.hv + h, 2);
+  __syncthreads();
+  if (s_last && warp == 0) {
+    __threadfence();
+    const int hh = lane >> 4, col = hh * VS + (lane & 15) * 4;  // lanes 0-15: half 0, 16-31: half 1
+    const float ss = __ldcg(rec + VS) + __ldcg(rec + kHalfFloats + VS);
+    const float r = rsqrtf(ss / (float)(2 * VS) + p.eps);
+    const float4 o4 = __ldcg(reinterpret_cast<const float4*>(rec + hh * kHalfFloats + (lane & 15) * 4));
+    const T* zr = static_cast<const T*>(p.z) + (int64_t)seq * p.z_t + (int64_t)h * p.z_h + col;
+    T* orow = static_cast<T*>(p.out) + (int64_t)seq * p.o_t + (int64_t)h * p.o_h + col;
+    const float ov[4] = {o4.x, o4.y, o4.z, o4.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      orow[j] = from_f32<T>(o4[j] * r * load_scalar(p.nw, vcol + j, p.nw_dt) * silu(to_f32<T>(zr[j])));
+      orow[j] = from_f32<T>(ov[j] * r * load_scalar(p.nw, col + j, p.nw_dt) * silu(to_f32<T>(zr[j])));
   }
-}
-
-template <typename T, typename TW, int W>
-cudaError_t launch_fused(const FusedParams& p, int64_t S, cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2, (unsigned)p.hv, (unsigned)S);
-  cfg.blockDim = dim3(kThreads);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = (unsigned)p.group;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gdn_decode_fused_kernel<T, TW, W>, p);
+  // the new state last: nothing after these stores waits for them
+#pragma unroll
+  for (int i = 0; i < NI; ++i) __stcs(reinterpret_cast<float4*>(S + (int64_t)(rg + RP * i) * p.ss_k), s[i]);
 }
 
 template <typename T, typename TW>
 cudaError_t launch_w(int w, const FusedParams& p, int64_t S, cudaStream_t st) {
+  const dim3 grid(2, (unsigned)p.hv, (unsigned)S);
   switch (w) {
-    case 2: return launch_fused<T, TW, 2>(p, S, st);
-    case 3: return launch_fused<T, TW, 3>(p, S, st);
-    case 4: return launch_fused<T, TW, 4>(p, S, st);
-    case 5: return launch_fused<T, TW, 5>(p, S, st);
-    case 6: return launch_fused<T, TW, 6>(p, S, st);
+    case 2: gdn_decode_fused_kernel<T, TW, 2><<<grid, kThreads, 0, st>>>(p); break;
+    case 3: gdn_decode_fused_kernel<T, TW, 3><<<grid, kThreads, 0, st>>>(p); break;
+    case 4: gdn_decode_fused_kernel<T, TW, 4><<<grid, kThreads, 0, st>>>(p); break;
+    case 5: gdn_decode_fused_kernel<T, TW, 5><<<grid, kThreads, 0, st>>>(p); break;
+    case 6: gdn_decode_fused_kernel<T, TW, 6><<<grid, kThreads, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
   }
-  return cudaErrorInvalidValue;
+  return cudaSuccess;
 }
+
+// Caller memory: the counters (conv [S, Hk], norm [S, Hv]; zero, and left at zero) and the
+// per-half records (no initial value needed).  Two buffers, so that records of one call never
+// land where another call's counters are.
+size_t counter_bytes(int64_t S, int64_t hk, int64_t hv) { return (size_t)S * (hk + hv) * sizeof(int); }
+size_t record_bytes(int64_t S, int64_t hv) { return (size_t)S * hv * 2 * kHalfFloats * sizeof(float); }
 
 }  // namespace
 }  // namespace mvb
+
+extern "C" int mvb_gated_deltanet_decode_workspace_sizes(int64_t n_seqs, int64_t num_k_heads, int64_t num_v_heads,
+                                                         size_t* counters_bytes, size_t* records_bytes) {
+  if (counters_bytes == nullptr || records_bytes == nullptr || n_seqs < 0 || num_k_heads <= 0 || num_v_heads <= 0)
+    MVB_FAIL(MVB_ERR_ARG, "gated_deltanet_decode_workspace_sizes: bad arguments");
+  *counters_bytes = mvb::counter_bytes(n_seqs, num_k_heads, num_v_heads);
+  *records_bytes = mvb::record_bytes(n_seqs, num_v_heads);
+  return MVB_OK;
+}
 
 extern "C" int mvb_gated_deltanet_decode(const mvb_tensor* qkv, const mvb_tensor* conv_weight, mvb_tensor* conv_state,
                                          const mvb_tensor* conv_state_indices, const mvb_tensor* a,
                                          const mvb_tensor* b, const mvb_tensor* a_log, const mvb_tensor* dt_bias,
                                          mvb_tensor* recurrent_state, const mvb_tensor* recurrent_state_indices,
                                          const mvb_tensor* z, const mvb_tensor* norm_weight, float norm_eps,
-                                         float scale, mvb_tensor* out, void* stream) {
+                                         float scale, mvb_tensor* out, void* counters, size_t counters_bytes,
+                                         void* records, size_t records_bytes, void* stream) {
   using namespace mvb;
   const char* op = "gated_deltanet_decode";
   int rc;
@@ -310,8 +321,6 @@ extern "C" int mvb_gated_deltanet_decode(const mvb_tensor* qkv, const mvb_tensor
   const int64_t hk = (dim - hv * vd) / (2 * kd);
   MVB_CHECK_ARG(hv % hk == 0, "%s: Hv (%lld) must be a multiple of Hk (%lld)", op, (long long)hv, (long long)hk);
   const int64_t group = hv / hk;
-  MVB_CHECK_SUPPORTED(group == 1 || group == 2 || group == 4, "%s: Hv / Hk must be 1, 2 or 4 (got %lld)", op,
-                      (long long)group);
   MVB_CHECK_SUPPORTED(Wd >= 2 && Wd <= 6, "%s: conv width must be 2..6", op);
   MVB_CHECK_ARG(conv_weight->shape[0] == dim && conv_state->shape[1] == Wd - 1 && conv_state->shape[2] == dim,
                 "%s: conv_weight [dim, W] / conv_state [S_max, W-1, dim] disagree with qkv", op);
@@ -346,6 +355,13 @@ extern "C" int mvb_gated_deltanet_decode(const mvb_tensor* qkv, const mvb_tensor
   MVB_CHECK_SUPPORTED(z->stride[2] == 1 && out->stride[2] == 1, "%s: z and out need a unit last stride", op);
   MVB_CHECK_SUPPORTED(S <= 65535 && hv <= 65535, "%s: at most 65535 sequences", op);
   if (S == 0) return MVB_OK;
+  MVB_CHECK_ARG(counters != nullptr && counters_bytes >= counter_bytes(S, hk, hv) &&
+                    (reinterpret_cast<uintptr_t>(counters) & 3) == 0,
+                "%s: needs %zu bytes of zero-initialised counters (mvb_gated_deltanet_decode_workspace_sizes)", op,
+                counter_bytes(S, hk, hv));
+  MVB_CHECK_ARG(records != nullptr && records_bytes >= record_bytes(S, hv) && (reinterpret_cast<uintptr_t>(records) & 15) == 0,
+                "%s: needs %zu bytes of 16-byte aligned record space (mvb_gated_deltanet_decode_workspace_sizes)", op,
+                record_bytes(S, hv));
 
   FusedParams p;
   memset(&p, 0, sizeof(p));
@@ -363,6 +379,9 @@ extern "C" int mvb_gated_deltanet_decode(const mvb_tensor* qkv, const mvb_tensor
   p.nw = norm_weight->data; p.nw_dt = norm_weight->dtype;
   p.out = out->data; p.o_t = out->stride[0]; p.o_h = out->stride[1];
   p.hk = (int)hk; p.hv = (int)hv; p.group = (int)group;
+  p.cnt_conv = static_cast<int*>(counters);
+  p.cnt_norm = p.cnt_conv + S * hk;
+  p.half_o = static_cast<float*>(records);
   p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)kd);
   p.eps = norm_eps;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -65,6 +65,9 @@ class GatedDeltaNet(nn.Module):
         self.in_proj_a = ColumnParallelLinear(hidden_size, num_v_heads, bias=False)
         self.recurrent_state: torch.Tensor = torch.empty(0)
         self.conv_state: torch.Tensor = torch.empty(0)
+        # decode through the one-kernel layer step (mvb_gated_deltanet_decode) instead of the
+        # conv-update, recurrence and gated-norm kernels
+        self.fused_decode = False
 
     def gates(self, a: torch.Tensor, b: torch.Tensor):
         """The layer's gate math in torch (the kernels form the same gates in-kernel from
@@ -92,9 +95,10 @@ class GatedDeltaNet(nn.Module):
             a, b = self.in_proj_a(x), self.in_proj_b(x)
         gate_inputs = (a, b, self.A_log, self.dt_bias)  # g, beta are formed inside the kernel
         zv = z.view(T, self.num_v_heads, self.v_head_dim)
-        if not is_prefill and fused_decode_supported(qkv, self.recurrent_state, self.num_k_heads, self.num_v_heads,
-                                                     zv):
-            # conv update + q/k norm + gates + recurrence + RMSNormGated in one kernel
+        if not is_prefill and self.fused_decode and fused_decode_supported(qkv, self.recurrent_state,
+                                                                           self.num_k_heads, self.num_v_heads, zv):
+            # conv update + q/k norm + gates + recurrence + RMSNormGated in one kernel (off by
+            # default: the separate kernels stream the state faster at serving batch sizes)
             o = gated_deltanet_decode(qkv, self.conv1d.weight, self.conv_state, conv_state_indices, a, b, self.A_log,
                                       self.dt_bias, self.recurrent_state, recurrent_state_indices, zv,
                                       self.norm.weight, self.norm.variance_epsilon)

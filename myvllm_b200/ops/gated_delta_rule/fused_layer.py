@@ -8,6 +8,8 @@ the input of ``out_proj``.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from ... import _lib
@@ -15,14 +17,12 @@ from ... import _lib
 
 def fused_decode_supported(qkv: torch.Tensor, recurrent_state: torch.Tensor, num_k_heads: int, num_v_heads: int,
                            z: torch.Tensor) -> bool:
-    """Layouts the fused kernel takes: 16-bit activations, K = V = 128, Hv / Hk in {1, 2, 4},
-    16-byte aligned projection rows with unit channel stride (the fused input projection's
-    output qualifies)."""
+    """Layouts the fused kernel takes: 16-bit activations, K = V = 128, 16-byte aligned
+    projection rows with unit channel stride (the fused input projection's output qualifies)."""
     return (qkv.is_cuda and qkv.dtype in (torch.bfloat16, torch.float16) and qkv.dim() == 2 and qkv.stride(1) == 1
             and qkv.stride(0) % 8 == 0 and qkv.data_ptr() % 16 == 0 and recurrent_state.dim() == 4
             and tuple(recurrent_state.shape[2:]) == (128, 128) and recurrent_state.dtype == torch.float32
-            and num_v_heads % num_k_heads == 0 and num_v_heads // num_k_heads in (1, 2, 4)
-            and z.stride(-1) == 1 and z.dtype == qkv.dtype)
+            and num_v_heads % num_k_heads == 0 and z.stride(-1) == 1 and z.dtype == qkv.dtype)
 
 
 def gated_deltanet_decode(qkv, conv_weight, conv_state, conv_state_indices, a, b, A_log, dt_bias, recurrent_state,
@@ -39,10 +39,19 @@ def gated_deltanet_decode(qkv, conv_weight, conv_state, conv_state_indices, a, b
     cidx = conv_state_indices if conv_state_indices.dtype == torch.int32 else conv_state_indices.int()
     ridx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
     scale = float(recurrent_state.shape[2] ** -0.5)
+    hk = (qkv.shape[1] - hv * vd) // (2 * recurrent_state.shape[2])
+    # counters (zero, and left at zero by every call) and the halves' partial outputs, in two
+    # buffers so that no call's records land on another call's counters
+    nc, nr = ctypes.c_size_t(), ctypes.c_size_t()
+    _lib.check("gated_deltanet_decode",
+               _lib.load().mvb_gated_deltanet_decode_workspace_sizes(S, hk, hv, ctypes.byref(nc), ctypes.byref(nr)))
+    cnt = _lib.workspace(qkv.device, nc.value, tag="gdn_decode_counters")
+    rec = _lib.workspace(qkv.device, nr.value, tag="gdn_decode_records")
     _lib.call("gated_deltanet_decode", "mvb_gated_deltanet_decode", _lib.desc(qkv), _lib.desc(conv_weight),
               _lib.desc(conv_state), _lib.desc(cidx), _lib.desc(a), _lib.desc(b), _lib.desc(A_log),
               _lib.desc(dt_bias), _lib.desc(recurrent_state), _lib.desc(ridx), _lib.desc(z),
-              _lib.desc(norm_weight), float(norm_eps), scale, _lib.desc(out), _lib.stream_of(qkv))
+              _lib.desc(norm_weight), float(norm_eps), scale, _lib.desc(out), cnt.data_ptr(), cnt.numel(),
+              rec.data_ptr(), rec.numel(), _lib.stream_of(qkv))
     return out
 
 

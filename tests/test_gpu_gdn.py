@@ -282,8 +282,8 @@ def test_gated_entry_points_match_torch_gates(prefill):
 def test_fused_layer_decode_matches_the_unfused_ops(hk, hv):
     """mvb_gated_deltanet_decode (conv update + q/k norm + gates + recurrence + RMSNormGated in
     one kernel) against the same layer step run as the separate library ops the layer used
-    before: the conv and recurrent states must come out bit for bit equal (same arithmetic),
-    the normed output within the bf16 bar.  Hv / Hk = 2 (the config-2/4 layout), 1 and 4;
+    before: the conv state bit for bit, the fp32 recurrent state to 1e-5 relative (the same
+    arithmetic, reduced in another order), the normed output within the bf16 bar.  Hv / Hk = 2 (the config-2/4 layout), 1 and 4;
     permuted state slots; projection rows taken as strided views of one fused GEMM output."""
     from myvllm_b200.layers.norm import RMSNormGated
     from myvllm_b200.ops.causal_conv1d import causal_conv1d_update
@@ -316,7 +316,9 @@ def test_fused_layer_decode_matches_the_unfused_ops(hk, hv):
     ref = norm(o, z)
     torch.cuda.synchronize()
     assert torch.equal(c1, c2), "conv state differs from the unfused conv update"
-    assert torch.equal(s1, s2), "recurrent state differs from the unfused recurrence"
+    # same arithmetic; the fused kernel reduces k^T S over the full 128-column row in another
+    # association order, so the fp32 states agree to rounding
+    assert state_rel_err(s1, s2) < 1e-5, "recurrent state differs from the unfused recurrence"
     assert_close(out, ref, what="fused decode output")
 
 
