@@ -1,4 +1,5 @@
-// RMS norms, HBM-bound, one warp per row held in registers as 16-byte vectors (D <= 2048):
+// RMS norms, HBM-bound, rows held in registers as 16-byte vectors (D <= 2048; a warp per row,
+// a block per row from D = 1024):
 //   gated:  out = x * rsqrt(mean(x^2) + eps) * weight * silu(gate)     (RMSNormGated,
 //           m/layers/norm.py:50-58, the GDN output norm)
 //   plain:  s = x (+ residual);  out = s * rsqrt(mean(s^2) + eps) * (weight [+ 1])
@@ -117,6 +118,54 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* x, Rows3 rx, T* r
   }
 }
 
+// The plain norm for wide rows (D >= 1024, e.g. the hidden states of a decode batch): one
+// 256-thread block per row, NV 16-byte vectors per thread, the sum of squares reduced across
+// the block's warps through shared memory.  A decode batch has few rows, so a warp per row
+// would leave most SMs idle with each warp's loads in series.
+template <typename T, typename TW, int NV>
+__global__ void __launch_bounds__(256) rmsnorm_wide_kernel(const T* x, Rows3 rx, T* res, Rows3 rr, const TW* w,
+                                                           T* out, Rows3 ro, int heads, int d, float eps,
+                                                           float w_offset) {
+  __shared__ float s_part[8];
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t ox = rx.at(row, heads), orr = rr.at(row, heads), oo = ro.at(row, heads);
+  float xv[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 256 + tid) * 8;
+    if (c < d) {
+      unpack8<T>(*reinterpret_cast<const uint4*>(x + ox + c), xv[i]);
+      if (res != nullptr) {
+        float r[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(res + orr + c), r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xv[i][j] += r[j];
+        *reinterpret_cast<uint4*>(res + orr + c) = pack8<T>(xv[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += xv[i][j] * xv[i][j];
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) s_part[wid] = ss;
+  __syncthreads();
+  ss = lane < 8 ? s_part[lane] : 0.f;
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)d + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 256 + tid) * 8;
+    if (c < d) {
+      float y[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = xv[i][j] * r * (to_f32<TW>(w[c + j]) + w_offset);
+      *reinterpret_cast<uint4*>(out + oo + c) = pack8<T>(y);
+    }
+  }
+}
+
 template <typename T, typename TW>
 void launch_plain(const mvb_tensor* x, mvb_tensor* res, const mvb_tensor* w, mvb_tensor* o, float eps, float w_off,
                   cudaStream_t st) {
@@ -130,6 +179,11 @@ void launch_plain(const mvb_tensor* x, mvb_tensor* res, const mvb_tensor* w, mvb
   const Rows3 rr = res ? rows3(res) : Rows3{0, 0};
   auto ws = static_cast<const TW*>(w->data);
   auto os = static_cast<T*>(o->data);
+  if (d >= 1024) {  // D <= 2048: one vector per thread of a block per row
+    rmsnorm_wide_kernel<T, TW, 1><<<(unsigned)rows, 256, 0, st>>>(xs, rows3(x), rs, rr, ws, os, rows3(o), heads, d,
+                                                                  eps, w_off);
+    return;
+  }
 #define MVB_NORM_CASE(N) \
   case N: rmsnorm_kernel<T, TW, N><<<blocks, 256, 0, st>>>(xs, rows3(x), rs, rr, ws, os, rows3(o), rows, heads, d, eps, w_off); break;
   switch (nv) {

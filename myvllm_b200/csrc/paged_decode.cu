@@ -318,6 +318,7 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeParams p)
   __shared__ float s_w[1024];
   __shared__ float s_tot;
   float M = -INFINITY;
+#pragma unroll 8
   for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, p.part_lse[(base + s) * 16 + r]);
   float tot = 0.f;
   for (int s = threadIdx.x; s < p.n_splits; s += blockDim.x) {
@@ -335,8 +336,17 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeParams p)
   T* o = static_cast<T*>(p.o);
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
     float acc = 0.f;
-    for (int s = 0; s < p.n_splits; ++s)
-      if (s_w[s] != 0.f) acc += s_w[s] * p.part_o[((base + s) * 16 + r) * D + c];
+    // eight splits' loads in flight before their adds (a split past the context has weight
+    // 0 and unwritten partials: the select keeps them out)
+    for (int s0 = 0; s0 < p.n_splits; s0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = s0 + j < p.n_splits ? p.part_o[((base + s0 + j) * 16 + r) * D + c] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < p.n_splits && s_w[s0 + j] != 0.f) acc += s_w[s0 + j] * v[j];
+    }
     const float gt = p.gate ? sigmoid_gate<T>(p, seq, hq, c) : 1.f;
     o[seq * p.so_s + hq * p.so_h + c] = from_f32<T>((tot > 0.f ? acc / tot : 0.f) * gt);
   }
