@@ -109,13 +109,20 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(const __gri
       *reinterpret_cast<uint4*>(static_cast<char*>(p.out) + i) = own;
       continue;
     }
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < p.world; ++r) {
-      const uint4 u = r == p.rank ? own : __ldcg(reinterpret_cast<const uint4*>(p.bufs[r] + slot_off + i));
-      float f[8];
-      unpack8<T>(u, f);
+    // every peer load is in flight before the first add: the NVLink round trips overlap
+    uint4 u[kMaxRanks];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] += f[j];
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < p.world) u[r] = r == p.rank ? own : __ldcg(reinterpret_cast<const uint4*>(p.bufs[r] + slot_off + i));
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r < p.world) {
+        float f[8];
+        unpack8<T>(u[r], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += f[j];
+      }
     }
     *reinterpret_cast<uint4*>(static_cast<char*>(p.out) + i) = pack8<T>(acc);
   }
