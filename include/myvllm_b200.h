@@ -197,6 +197,32 @@ int mvb_paged_attention_decode_gated(const mvb_tensor* q, const mvb_tensor* k_ca
                                      int block_size, int64_t max_context_len, const mvb_tensor* gate, mvb_tensor* o,
                                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Context-split decode, for tensor parallelism past the number of kv heads, where the
+ * reference asserts (m/layers/full_attention.py:34-35 requires num_kv_heads % tp == 0).
+ * The n_parts ranks that hold copies of a kv head each attend, for all q heads of that kv
+ * head, over every n_parts-th split of each context (splits s with s % n_parts == part),
+ * instead of all of them attending over the whole context.  Out: o_part [S, Hq, Dv] fp32
+ * (contiguous), this part's attention normalised within the part, and lse_part [S, Hq]
+ * fp32 (contiguous), its log2-sum-exp (-inf where the part holds no keys).  workspace: at
+ * least mvb_paged_attention_decode_part_workspace_size(...) bytes (required).  Other
+ * arguments as mvb_paged_attention_decode. */
+size_t mvb_paged_attention_decode_part_workspace_size(int64_t n_seqs, int64_t num_kv_heads, int64_t head_v_dim,
+                                                      int64_t max_context_len, int n_parts);
+int mvb_paged_attention_decode_part(const mvb_tensor* q, const mvb_tensor* k_cache, const mvb_tensor* v_cache,
+                                    const mvb_tensor* block_tables, const mvb_tensor* context_lens, float scale,
+                                    int block_size, int64_t max_context_len, int part, int n_parts,
+                                    mvb_tensor* o_part, mvb_tensor* lse_part, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
+/* This rank's share of the context-split attention: o = o_part * w (* sigmoid(gate)),
+ * w = 2^(lse_own - M) / sum_j 2^(lse_j - M) over the parts j of lse_parts [n_parts, S, Hq]
+ * (fp32, rows contiguous; lse_own = lse_parts[part]), M their max.  The shares of all parts
+ * sum to the attention over the whole context, so each rank projects its share and the
+ * all-reduce after the output projection (m/layers/linear.py:159-164) adds them.  o [S, Hq,
+ * Dv] bf16/fp16; gate as in mvb_paged_attention_decode_gated, or NULL. */
+int mvb_attention_merge_parts(const mvb_tensor* o_part, const mvb_tensor* lse_parts, int part, const mvb_tensor* gate,
+                              mvb_tensor* o, void* stream);
+
 /* Allocation-free variant of mvb_paged_attention_decode (no counterpart in the reference).
  * For callers that may not allocate device memory when they decode: the split-KV partial
  * results go to a fixed 16 MiB array in the library's device image instead of a caller

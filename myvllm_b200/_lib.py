@@ -77,6 +77,11 @@ SIGNATURES = {
                                                         ctypes.c_int64, _T, _T, _P, ctypes.c_size_t, _P]),
     "mvb_paged_attention_decode_noalloc": (ctypes.c_int, [_T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int,
                                                           ctypes.c_int64, _T, _P]),
+    "mvb_paged_attention_decode_part_workspace_size": (ctypes.c_size_t, [ctypes.c_int64] * 4 + [ctypes.c_int]),
+    "mvb_paged_attention_decode_part": (ctypes.c_int, [_T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int,
+                                                       ctypes.c_int64, ctypes.c_int, ctypes.c_int, _T, _T, _P,
+                                                       ctypes.c_size_t, _P]),
+    "mvb_attention_merge_parts": (ctypes.c_int, [_T, _T, ctypes.c_int, _T, _T, _P]),
     "mvb_paged_attention_prefill": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int, _T, _P]),
     "mvb_store_kvcache": (ctypes.c_int, [_T, _T, _T, _T, _T, _P]),
     "mvb_rmsnorm_gated": (ctypes.c_int, [_T, _T, _T, ctypes.c_float, _T, _P]),

@@ -30,6 +30,11 @@ struct DecodeParams {
   int64_t sgt_s, sgt_h;
   float* part_o;     // [S, Hkv, n_splits, 16, Dv] fp32, or null when n_splits == 1
   float* part_lse;   // [S, Hkv, n_splits, 16]
+  // Context parts (a kv head's context shared out among n_parts ranks): this call runs the
+  // splits s with s % n_parts == part and leaves their merge, normalised within the part, in
+  // o_part [S, Hq, Dv] fp32 with its log2-sum-exp in lse_part [S, Hq].  n_parts == 1: off.
+  int part, n_parts;
+  float *o_part, *lse_part;
   int64_t sq_s, sq_h, so_s, so_h;
   int64_t skc_b, skc_t, skc_h, svc_b, svc_t, svc_h;
   int64_t sbt_s, sbt_b;
@@ -119,7 +124,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams 
   extern __shared__ __align__(128) char smem[];
   char* sQ = smem + NS * SM::kStageBytes;
   int* spages = reinterpret_cast<int*>(sQ + SM::kQBytes);
-  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+  const int split = blockIdx.x * p.n_parts + p.part, kvh = blockIdx.y, seq = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ctx = p.ctx[seq];
   const int t_begin = split * p.split_len;
@@ -127,10 +132,10 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams 
   const int G = p.group;
 
   if (t_begin >= t_end) {
-    if (p.n_splits > 1 && tid < 16) {
+    if (p.part_o != nullptr && tid < 16) {
       const int64_t pi = ((int64_t)seq * p.hkv + kvh) * p.n_splits + split;
       p.part_lse[pi * 16 + tid] = -INFINITY;
-    } else if (p.n_splits == 1) {  // empty context: zeros
+    } else if (p.part_o == nullptr) {  // empty context: zeros
       T* o = static_cast<T*>(p.o);
       for (int i = tid; i < G * D; i += kWarps * 32)
         o[seq * p.so_s + (kvh * G + i / D) * p.so_h + i % D] = from_f32<T>(0.f);
@@ -297,7 +302,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams 
       O += f * red[(w * 16 + r) * D + c];
     }
     const float out = L > 0.f ? O / L : 0.f;
-    if (p.n_splits == 1) {
+    if (p.part_o == nullptr) {
       T* o = static_cast<T*>(p.o);
       const float gt = p.gate ? sigmoid_gate<T>(p, seq, kvh * G + r, c) : 1.f;
       o[seq * p.so_s + (kvh * G + r) * p.so_h + c] = from_f32<T>(out * gt);
@@ -315,20 +320,22 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeParams p)
   const int seq = blockIdx.y, hq = blockIdx.x;
   const int kvh = hq / p.group, r = hq % p.group;
   const int64_t base = ((int64_t)seq * p.hkv + kvh) * p.n_splits;
+  // the splits this call ran: s = part + i n_parts (all of them, in order, without parts)
+  const int n_own = p.part < p.n_splits ? (p.n_splits - p.part + p.n_parts - 1) / p.n_parts : 0;
   __shared__ float s_w[1024];
   __shared__ float s_tot;
   float M = -INFINITY;
 #pragma unroll 8
-  for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, p.part_lse[(base + s) * 16 + r]);
+  for (int i = 0; i < n_own; ++i) M = fmaxf(M, p.part_lse[(base + p.part + i * p.n_parts) * 16 + r]);
   float tot = 0.f;
-  for (int s = threadIdx.x; s < p.n_splits; s += blockDim.x) {
-    const float l = p.part_lse[(base + s) * 16 + r];
+  for (int i = threadIdx.x; i < n_own; i += blockDim.x) {
+    const float l = p.part_lse[(base + p.part + i * p.n_parts) * 16 + r];
     const float w = l == -INFINITY ? 0.f : exp2f(l - M);
-    s_w[s] = w;
+    s_w[i] = w;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.n_splits; ++s) tot += s_w[s];
+    for (int i = 0; i < n_own; ++i) tot += s_w[i];
     s_tot = tot;
   }
   __syncthreads();
@@ -338,17 +345,51 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeParams p)
     float acc = 0.f;
     // eight splits' loads in flight before their adds (a split past the context has weight
     // 0 and unwritten partials: the select keeps them out)
-    for (int s0 = 0; s0 < p.n_splits; s0 += 8) {
+    for (int i0 = 0; i0 < n_own; i0 += 8) {
       float v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        v[j] = s0 + j < p.n_splits ? p.part_o[((base + s0 + j) * 16 + r) * D + c] : 0.f;
+        v[j] = i0 + j < n_own ? p.part_o[((base + p.part + (i0 + j) * p.n_parts) * 16 + r) * D + c] : 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (s0 + j < p.n_splits && s_w[s0 + j] != 0.f) acc += s_w[s0 + j] * v[j];
+        if (i0 + j < n_own && s_w[i0 + j] != 0.f) acc += s_w[i0 + j] * v[j];
     }
-    const float gt = p.gate ? sigmoid_gate<T>(p, seq, hq, c) : 1.f;
-    o[seq * p.so_s + hq * p.so_h + c] = from_f32<T>((tot > 0.f ? acc / tot : 0.f) * gt);
+    const float out = tot > 0.f ? acc / tot : 0.f;
+    if (p.o_part != nullptr) {  // this part's share, normalised within the part
+      const int64_t oi = (int64_t)seq * p.hq + hq;
+      p.o_part[oi * D + c] = out;
+      if (c == 0) p.lse_part[oi] = tot > 0.f ? M + log2f(tot) : -INFINITY;
+    } else {
+      const float gt = p.gate ? sigmoid_gate<T>(p, seq, hq, c) : 1.f;
+      o[seq * p.so_s + hq * p.so_h + c] = from_f32<T>(out * gt);
+    }
+  }
+}
+
+// The parts of a context split merged: o = o_part w (sigmoid(gate)), w = 2^(lse_own - M) /
+// sum_j 2^(lse_j - M) over the parts j, M their max.  Summed over the parts, these outputs
+// are the attention over the whole context; each part's output goes through the output
+// projection on its own rank and the all-reduce after it adds them.  One CTA per (seq, q-head).
+template <typename T, int D>
+__global__ void __launch_bounds__(128) attention_parts_merge_kernel(const float* o_part, const float* lse_parts,
+                                                                    int64_t sl_part, int n_parts, int part,
+                                                                    const T* gate, int64_t sg_s, int64_t sg_h, T* o,
+                                                                    int64_t so_s, int64_t so_h, int hq) {
+  const int seq = blockIdx.y, h = blockIdx.x;
+  const int64_t oi = (int64_t)seq * hq + h;
+  float M = -INFINITY;
+  for (int j = 0; j < n_parts; ++j) M = fmaxf(M, lse_parts[j * sl_part + oi]);
+  float L = 0.f;
+  for (int j = 0; j < n_parts; ++j) {
+    const float l = lse_parts[j * sl_part + oi];
+    L += l == -INFINITY ? 0.f : exp2f(l - M);
+  }
+  const float own = lse_parts[part * sl_part + oi];
+  const float w = (L > 0.f && own != -INFINITY) ? exp2f(own - M) / L : 0.f;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float g = 1.f;
+    if (gate != nullptr) g = 1.f / (1.f + __expf(-to_f32<T>(gate[seq * sg_s + h * sg_h + c])));
+    o[seq * so_s + h * so_h + c] = from_f32<T>(w == 0.f ? 0.f : o_part[oi * D + c] * w * g);
   }
 }
 
@@ -357,12 +398,14 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeParams p)
 constexpr int kMaxSplits = 1024;
 
 // Chooses the split length (a multiple of the tile) for a context bound and batch.
-inline int decode_split_len(int64_t n_seqs, int64_t hkv, int64_t max_ctx, int64_t max_splits) {
+// With a context split over n_parts ranks each rank runs 1 / n_parts of the splits, so
+// there are n_parts times as many.
+inline int decode_split_len(int64_t n_seqs, int64_t hkv, int64_t max_ctx, int64_t max_splits, int64_t n_parts = 1) {
   if (max_splits <= 1) return (int)(((max_ctx + kTile - 1) / kTile) * kTile);  // one split: the whole context
   const int64_t per = n_seqs * hkv;
   // aim for >= 8 CTAs per SM of work (16 measured the same at config 4; 32 and more were
   // 45% slower)
-  int64_t target = (8LL * 148 + per - 1) / (per > 0 ? per : 1);
+  int64_t target = (8LL * 148 * n_parts + per - 1) / (per > 0 ? per : 1);
   int64_t split = (max_ctx + target - 1) / (target > 0 ? target : 1);
   split = ((split + kTile - 1) / kTile) * kTile;
   if (split < 512) split = 512;
@@ -370,8 +413,8 @@ inline int decode_split_len(int64_t n_seqs, int64_t hkv, int64_t max_ctx, int64_
   return (int)split;
 }
 
-size_t decode_workspace_bytes(int64_t n_seqs, int64_t hkv, int64_t dv, int n_splits) {
-  if (n_splits <= 1) return 0;
+size_t decode_workspace_bytes(int64_t n_seqs, int64_t hkv, int64_t dv, int n_splits, bool parts = false) {
+  if (n_splits <= 1 && !parts) return 0;
   return (size_t)n_seqs * hkv * n_splits * 16 * (dv + 1) * sizeof(float);
 }
 
@@ -384,9 +427,12 @@ int launch_decode(DecodeParams& p, int64_t n_seqs, cudaStream_t st) {
   const int smem = DecodeSmem<D>::kBytes;
   static unsigned long long attr_mask = 0;
   ensure_smem_attr(paged_decode_kernel<T, D>, smem, attr_mask);
-  dim3 grid(p.n_splits, p.hkv, (unsigned)n_seqs);
-  paged_decode_kernel<T, D><<<grid, kWarps * 32, smem, st>>>(p);
-  if (p.n_splits > 1) {
+  const int n_own = p.part < p.n_splits ? (p.n_splits - p.part + p.n_parts - 1) / p.n_parts : 0;
+  if (n_own > 0) {
+    dim3 grid(n_own, p.hkv, (unsigned)n_seqs);
+    paged_decode_kernel<T, D><<<grid, kWarps * 32, smem, st>>>(p);
+  }
+  if (p.part_o != nullptr) {
     dim3 g2(p.hq, (unsigned)n_seqs);
     paged_decode_merge_kernel<T, D><<<g2, 128, 0, st>>>(p);
   }
@@ -398,7 +444,10 @@ int launch_decode(DecodeParams& p, int64_t n_seqs, cudaStream_t st) {
 int run_paged_decode(const char* op, const mvb_tensor* q, const mvb_tensor* kc, const mvb_tensor* vc,
                      const mvb_tensor* bt, const mvb_tensor* ctx, float scale, int block_size, int64_t max_ctx,
                      mvb_tensor* o, void* ws, size_t ws_bytes, int64_t max_splits, cudaStream_t st,
-                     const mvb_tensor* gate = nullptr) {
+                     const mvb_tensor* gate = nullptr, int part = 0, int n_parts = 1,
+                     mvb_tensor* lse_part = nullptr) {
+  // lse_part set: a context part (o is then the part's fp32 output [S, Hq, Dv], contiguous)
+  const bool parts = lse_part != nullptr;
   int rc;
   if ((rc = check_tensor(q, op, "q", 3)) || (rc = check_tensor(kc, op, "k_cache", 4)) ||
       (rc = check_tensor(vc, op, "v_cache", 4)) || (rc = check_tensor(bt, op, "block_tables", 2)) ||
@@ -414,7 +463,17 @@ int run_paged_decode(const char* op, const mvb_tensor* q, const mvb_tensor* kc, 
   MVB_CHECK_ARG(o->shape[0] == S && o->shape[1] == hq && o->shape[2] == dv, "%s: o must be [S, Hq, Dv]", op);
   MVB_CHECK_ARG(bt->shape[0] >= S && ctx->shape[0] >= S && bt->dtype == MVB_I32 && ctx->dtype == MVB_I32,
                 "%s: block_tables [S, max_blocks] and context_lens [S] must be int32", op);
-  MVB_CHECK_ARG(q->dtype == kc->dtype && q->dtype == vc->dtype && q->dtype == o->dtype, "%s: dtype mismatch", op);
+  MVB_CHECK_ARG(q->dtype == kc->dtype && q->dtype == vc->dtype && (parts ? o->dtype == MVB_F32 : q->dtype == o->dtype),
+                "%s: dtype mismatch", op);
+  if (parts) {
+    if ((rc = check_tensor(lse_part, op, "lse_part", 2))) return rc;
+    MVB_CHECK_ARG(n_parts >= 1 && part >= 0 && part < n_parts, "%s: part %d of %d", op, part, n_parts);
+    MVB_CHECK_ARG(lse_part->shape[0] == S && lse_part->shape[1] == hq && lse_part->dtype == MVB_F32,
+                  "%s: lse_part must be [S, Hq] fp32", op);
+    MVB_CHECK_SUPPORTED(o->stride[0] == hq * dv && o->stride[1] == dv && lse_part->stride[0] == hq &&
+                            lse_part->stride[1] == 1,
+                        "%s: o_part and lse_part must be contiguous", op);
+  }
   MVB_CHECK_SUPPORTED(q->dtype == MVB_BF16 || q->dtype == MVB_F16, "%s: q/k/v must be bf16 or fp16", op);
   MVB_CHECK_SUPPORTED(d == dv && (d == 64 || d == 128 || d == 256), "%s: head dim must be 64, 128 or 256", op);
   MVB_CHECK_SUPPORTED(hq / hkv <= 16, "%s: at most 16 query heads per kv head", op);
@@ -448,16 +507,22 @@ int run_paged_decode(const char* op, const mvb_tensor* q, const mvb_tensor* kc, 
   p.max_blocks = (int)bt->shape[1];
   p.scale_log2 = scale * 1.4426950408889634f;
 
-  int split = decode_split_len(S, hkv, max_ctx, max_splits);
+  int split = decode_split_len(S, hkv, max_ctx, max_splits, parts ? n_parts : 1);
   int n_splits = (int)((max_ctx + split - 1) / split);
-  if (ws == nullptr || ws_bytes < decode_workspace_bytes(S, hkv, dv, n_splits)) {
+  if (ws == nullptr || ws_bytes < decode_workspace_bytes(S, hkv, dv, n_splits, parts)) {
+    if (parts)
+      MVB_FAIL(MVB_ERR_ARG, "%s: the workspace needs %zu bytes", op, decode_workspace_bytes(S, hkv, dv, n_splits, true));
     n_splits = 1;
     split = (int)max_ctx;
   }
   p.n_splits = n_splits;
   p.split_len = split;
-  p.part_o = n_splits > 1 ? static_cast<float*>(ws) : nullptr;
-  p.part_lse = n_splits > 1 ? p.part_o + (size_t)S * hkv * n_splits * 16 * dv : nullptr;
+  p.part_o = (n_splits > 1 || parts) ? static_cast<float*>(ws) : nullptr;
+  p.part_lse = p.part_o != nullptr ? p.part_o + (size_t)S * hkv * n_splits * 16 * dv : nullptr;
+  p.part = parts ? part : 0;
+  p.n_parts = parts ? n_parts : 1;
+  p.o_part = parts ? static_cast<float*>(o->data) : nullptr;
+  p.lse_part = parts ? static_cast<float*>(lse_part->data) : nullptr;
 
   if (q->dtype == MVB_BF16) {
     switch (d) {
@@ -506,6 +571,79 @@ extern "C" int mvb_paged_attention_decode_gated(const mvb_tensor* q, const mvb_t
   return mvb::run_paged_decode("paged_attention_decode_gated", q, k_cache, v_cache, block_tables, context_lens,
                                scale, block_size, max_context_len, o, workspace, workspace_bytes, mvb::kMaxSplits,
                                static_cast<cudaStream_t>(stream), gate);
+}
+
+// ---------------------------------------------------------------------------------------
+// Context-split decode: the ranks that hold copies of one kv head (tensor parallelism past
+// the number of kv heads) each attend over a share of every context.
+extern "C" size_t mvb_paged_attention_decode_part_workspace_size(int64_t n_seqs, int64_t num_kv_heads,
+                                                                 int64_t head_v_dim, int64_t max_context_len,
+                                                                 int n_parts) {
+  if (n_seqs <= 0 || num_kv_heads <= 0 || max_context_len <= 0 || n_parts < 1) return 0;
+  const int split = mvb::decode_split_len(n_seqs, num_kv_heads, max_context_len, mvb::kMaxSplits, n_parts);
+  const int n_splits = (int)((max_context_len + split - 1) / split);
+  return mvb::decode_workspace_bytes(n_seqs, num_kv_heads, head_v_dim, n_splits, true);
+}
+
+extern "C" int mvb_paged_attention_decode_part(const mvb_tensor* q, const mvb_tensor* k_cache,
+                                               const mvb_tensor* v_cache, const mvb_tensor* block_tables,
+                                               const mvb_tensor* context_lens, float scale, int block_size,
+                                               int64_t max_context_len, int part, int n_parts, mvb_tensor* o_part,
+                                               mvb_tensor* lse_part, void* workspace, size_t workspace_bytes,
+                                               void* stream) {
+  if (lse_part == nullptr) MVB_FAIL(MVB_ERR_ARG, "paged_attention_decode_part: lse_part is NULL");
+  return mvb::run_paged_decode("paged_attention_decode_part", q, k_cache, v_cache, block_tables, context_lens, scale,
+                               block_size, max_context_len, o_part, workspace, workspace_bytes, mvb::kMaxSplits,
+                               static_cast<cudaStream_t>(stream), nullptr, part, n_parts, lse_part);
+}
+
+extern "C" int mvb_attention_merge_parts(const mvb_tensor* o_part, const mvb_tensor* lse_parts, int part,
+                                         const mvb_tensor* gate, mvb_tensor* o, void* stream) {
+  using namespace mvb;
+  const char* op = "attention_merge_parts";
+  int rc;
+  if ((rc = check_tensor(o_part, op, "o_part", 3)) || (rc = check_tensor(lse_parts, op, "lse_parts", 3)) ||
+      (rc = check_tensor(o, op, "o", 3)) || (gate && (rc = check_tensor(gate, op, "gate", 3))))
+    return rc;
+  const int64_t S = o_part->shape[0], hq = o_part->shape[1], d = o_part->shape[2];
+  const int n_parts = (int)lse_parts->shape[0];
+  MVB_CHECK_ARG(o_part->dtype == MVB_F32 && lse_parts->dtype == MVB_F32, "%s: o_part and lse_parts must be fp32", op);
+  MVB_CHECK_ARG(lse_parts->shape[1] == S && lse_parts->shape[2] == hq, "%s: lse_parts must be [n_parts, S, Hq]", op);
+  MVB_CHECK_ARG(part >= 0 && part < n_parts, "%s: part %d of %d", op, part, n_parts);
+  MVB_CHECK_ARG(o->shape[0] == S && o->shape[1] == hq && o->shape[2] == d &&
+                    (o->dtype == MVB_BF16 || o->dtype == MVB_F16),
+                "%s: o must be [S, Hq, Dv] bf16 or fp16", op);
+  MVB_CHECK_ARG(!gate || (gate->shape[0] == S && gate->shape[1] == hq && gate->shape[2] == d &&
+                          gate->dtype == o->dtype),
+                "%s: gate must be [S, Hq, Dv] in the dtype of o", op);
+  MVB_CHECK_SUPPORTED(d == 64 || d == 128 || d == 256, "%s: head dim must be 64, 128 or 256", op);
+  MVB_CHECK_SUPPORTED(o_part->stride[0] == hq * d && o_part->stride[1] == d && o_part->stride[2] == 1 &&
+                          lse_parts->stride[1] == hq && lse_parts->stride[2] == 1 && o->stride[2] == 1 &&
+                          (!gate || gate->stride[2] == 1) && S <= 65535,
+                      "%s: o_part and the rows of lse_parts must be contiguous", op);
+  if (S == 0 || hq == 0) return MVB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)hq, (unsigned)S);
+  const float* op_ = static_cast<const float*>(o_part->data);
+  const float* lp = static_cast<const float*>(lse_parts->data);
+  const int64_t sg_s = gate ? gate->stride[0] : 0, sg_h = gate ? gate->stride[1] : 0;
+#define MVB_MERGE_CASE(T, DD)                                                                                     \
+  attention_parts_merge_kernel<T, DD><<<grid, 128, 0, st>>>(op_, lp, lse_parts->stride[0], n_parts, part,        \
+                                                           gate ? static_cast<const T*>(gate->data) : nullptr,  \
+                                                           sg_s, sg_h, static_cast<T*>(o->data), o->stride[0],   \
+                                                           o->stride[1], (int)hq)
+  if (o->dtype == MVB_BF16) {
+    if (d == 64) MVB_MERGE_CASE(__nv_bfloat16, 64);
+    else if (d == 128) MVB_MERGE_CASE(__nv_bfloat16, 128);
+    else MVB_MERGE_CASE(__nv_bfloat16, 256);
+  } else {
+    if (d == 64) MVB_MERGE_CASE(__half, 64);
+    else if (d == 128) MVB_MERGE_CASE(__half, 128);
+    else MVB_MERGE_CASE(__half, 256);
+  }
+#undef MVB_MERGE_CASE
+  MVB_CHECK_LAUNCH(op);
+  return MVB_OK;
 }
 
 // ---------------------------------------------------------------------------------------

@@ -165,7 +165,8 @@ class HybridDecodeStack:
         """HBM bytes one step must move on this rank: the K/V read, the states read and
         written, and the weights read once."""
         hkv = self.fa[0].num_kv_heads if self.fa else 0
-        kv = sum(self.ctx_lens) * len(self.fa) * hkv * FA_D * 2 * 2
+        share = self.fa[0].kv_share if self.fa else 1  # a context-split rank reads 1 / share of it
+        kv = sum(self.ctx_lens) * len(self.fa) * hkv * FA_D * 2 * 2 // share
         states = 2 * self.lac.recurrent_cache.numel() * 4 + 2 * self.lac.conv_cache.numel() * 2
         weights = sum(p.numel() * p.element_size() for _, m in self.layers for p in m.parameters())
         return {"kv": kv, "states": states, "weights": weights, "total": kv + states + weights}

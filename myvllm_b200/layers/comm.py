@@ -177,6 +177,16 @@ def fused_linear(x: torch.Tensor, w: torch.Tensor, group=None):
     return f(x, w)
 
 
+def all_gather_block(t: torch.Tensor, block: int) -> torch.Tensor:
+    """``[block, *t.shape]``: ``t`` from each rank of this rank's block of ``block``
+    consecutive ranks (NCCL all-gather over the world; the blocks are small statistics)."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, t.contiguous())
+    first = (rank // block) * block
+    return out[first:first + block]
+
+
 def all_reduce(t: torch.Tensor, group=None) -> torch.Tensor:
     """Sum of ``t`` over the ranks of ``group``; returns the result (``t`` itself when NCCL
     reduces it in place)."""

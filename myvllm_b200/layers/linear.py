@@ -166,6 +166,9 @@ class RowParallelLinear(Linear):
     def __init__(self, input_size: int, output_size: int, bias: bool = False, prefix: str = ""):
         self.tp_rank, self.tp_size = tp_rank_size()
         assert input_size % self.tp_size == 0
+        # the input slice this rank loads; tp_rank/tp_size set the all-reduce, and a layer
+        # may widen that to more ranks than the slicing (context-split attention)
+        self.shard_rank = self.tp_rank
         super().__init__(input_size // self.tp_size, output_size, bias, prefix)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -185,4 +188,4 @@ class RowParallelLinear(Linear):
         if param.dim() == 1:  # bias: replicated
             param.data.copy_(loaded_weights)
             return
-        param.data.copy_(loaded_weights.narrow(1, self.tp_rank * self.input_size, self.input_size))
+        param.data.copy_(loaded_weights.narrow(1, self.shard_rank * self.input_size, self.input_size))

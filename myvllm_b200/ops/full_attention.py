@@ -73,6 +73,52 @@ def paged_flash_attention_decode(
     return o
 
 
+def paged_flash_attention_decode_part(
+    q: torch.Tensor,  # (seq_cnt, num_q_heads, qk_head_dim): every q head of the kv heads in the cache
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: float,
+    block_size: int,
+    part: int,
+    n_parts: int,
+    max_context_len: int | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Context-split decode (no counterpart in the reference, which asserts TP <= Hkv): this
+    rank's part of the attention over every ``n_parts``-th split of each context.  Returns
+    ``(o_part [seq_cnt, num_q_heads, v_head_dim] fp32, lse_part [seq_cnt, num_q_heads] fp32)``,
+    normalised within the part; :func:`merge_attention_parts` weighs it against the others."""
+    _lib.require_cuda("paged_flash_attention_decode_part", q, k_cache, v_cache, block_tables, context_lens)
+    seq_cnt, num_q_heads, _ = q.shape
+    num_kv_heads, v_head_dim = v_cache.shape[-2:]
+    o = torch.empty(seq_cnt, num_q_heads, v_head_dim, dtype=torch.float32, device=q.device)
+    lse = torch.empty(seq_cnt, num_q_heads, dtype=torch.float32, device=q.device)
+    bound = int(max_context_len) if max_context_len else int(block_tables.shape[1]) * int(block_size)
+    nbytes = _lib.load().mvb_paged_attention_decode_part_workspace_size(seq_cnt, num_kv_heads, v_head_dim, bound,
+                                                                       int(n_parts))
+    ws = _lib.workspace(q.device, nbytes, tag="paged_decode_part")
+    _lib.call("paged_flash_attention_decode_part", "mvb_paged_attention_decode_part", _lib.desc(q), _lib.desc(k_cache),
+              _lib.desc(v_cache), _lib.desc(_i32(block_tables)), _lib.desc(_i32(context_lens)), float(scale),
+              int(block_size), bound, int(part), int(n_parts), _lib.desc(o), _lib.desc(lse), ws.data_ptr(), ws.numel(),
+              _lib.stream_of(q))
+    return o, lse
+
+
+def merge_attention_parts(o_part: torch.Tensor, lse_parts: torch.Tensor, part: int,
+                          output_gate: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16
+                          ) -> torch.Tensor:
+    """This part's weighted share of the context-split attention (``* sigmoid(output_gate)``):
+    ``lse_parts`` [n_parts, seq_cnt, num_q_heads] holds every part's log2-sum-exp.  The shares
+    of all parts sum to the attention over the whole context."""
+    _lib.require_cuda("merge_attention_parts", o_part, lse_parts)
+    o = torch.empty(o_part.shape, dtype=output_gate.dtype if output_gate is not None else out_dtype,
+                    device=o_part.device)
+    _lib.call("merge_attention_parts", "mvb_attention_merge_parts", _lib.desc(o_part), _lib.desc(lse_parts), int(part),
+              _lib.desc(output_gate) if output_gate is not None else None, _lib.desc(o), _lib.stream_of(o_part))
+    return o
+
+
 def paged_flash_attention_prefill(
     q: torch.Tensor,  # (total_tokens, num_q_heads, qk_head_dim)
     k_cache: torch.Tensor,  # (max_num_cached_blocks, block_size, num_kv_heads, qk_head_dim)

@@ -43,17 +43,39 @@ def test_sharded_stack_is_a_slice_of_the_full_stack(full, world):
         want_c = torch.cat([c[..., r * qs:(r + 1) * qs], c[..., 2048 + r * qs:2048 + (r + 1) * qs],
                             c[..., 4096 + r * vs:4096 + (r + 1) * vs]], -1)
         assert torch.equal(part.lac.conv_cache, want_c)
-        # attention layer: q heads split; KV heads split at tp <= 2, replicated beyond
+        # attention layer: KV heads split at tp <= 2 with the q heads; beyond, each kv head is
+        # copied to the tp / 2 ranks of its share, which split its context and hold all its
+        # q heads (q/gate rows, o_proj columns)
         a_full, a_part = full.fa[0], part.fa[0]
-        hq = 16 // world
-        assert torch.equal(a_part.q_proj.weight, a_full.q_proj.weight[r * hq * 512:(r + 1) * hq * 512])
-        kv_heads = [r] if world == 2 else [r * 2 // world]
+        h = r if world == 2 else r * 2 // world
+        share = max(1, world // 2)
+        assert (a_part.kv_share, a_part.kv_part) == (share, r % share)
+        hq = 8 if share > 1 else 16 // world
+        first_q = h * 8 if share > 1 else r * hq
+        assert torch.equal(a_part.q_proj.weight, a_full.q_proj.weight[first_q * 512:(first_q + hq) * 512])
         assert a_part.num_kv_heads == 1
-        h = kv_heads[0]
         assert torch.equal(a_part.k_proj.weight, a_full.k_proj.weight[h * 256:(h + 1) * 256])
         assert torch.equal(part.kv.k[..., 0, :], full.kv.k[..., h, :])
         assert torch.equal(part.kv.v[..., 0, :], full.kv.v[..., h, :])
-        assert torch.equal(a_part.o_proj.weight, a_full.o_proj.weight[:, r * hq * 256:(r + 1) * hq * 256])
+        assert torch.equal(a_part.o_proj.weight, a_full.o_proj.weight[:, first_q * 256:(first_q + hq) * 256])
+        assert (a_part.o_proj.tp_rank, a_part.o_proj.tp_size) == (r, world)  # the all-reduce spans every rank
+        if share > 1:
+            assert part.bytes_per_step()["kv"] * share == sum(CTX) * 1 * 1 * 256 * 2 * 2
+
+
+def test_replicated_kv_heads_without_context_split():
+    from myvllm_b200.layers.full_attention import GatedAttention
+
+    GatedAttention.context_split = False
+    try:
+        full, part = _stack((0, 1)), _stack((3, 4))
+    finally:
+        GatedAttention.context_split = True
+    a_full, a_part = full.fa[0], part.fa[0]
+    assert (a_part.kv_share, a_part.num_q_heads) == (1, 4)
+    assert torch.equal(a_part.q_proj.weight, a_full.q_proj.weight[12 * 512:16 * 512])
+    assert torch.equal(a_part.o_proj.weight, a_full.o_proj.weight[:, 12 * 256:16 * 256])
+    assert torch.equal(part.kv.k[..., 0, :], full.kv.k[..., 1, :])
 
 
 def test_bytes_per_step_counts_kv_states_and_weights(full):

@@ -230,3 +230,29 @@ def test_paged_decode_output_gate(ctx_lens):
     gated = paged_flash_attention_decode(q, kc, vc, bt.to(dev), ctx, 1 / 16, 256, output_gate=gate)
     ref = plain.float() * torch.sigmoid(gate.float())
     assert_close(gated, ref, what="gated decode")
+
+
+@pytest.mark.parametrize("n_parts", [2, 4])
+@pytest.mark.parametrize("ctx_lens", [[3000, 17, 256, 8000, 33000], [1, 40]])
+def test_paged_decode_context_parts(n_parts, ctx_lens):
+    """Context-split decode (TP past the kv head count): each part attends over every
+    n_parts-th split of each context; merged with the gathered log-sum-exps and the output
+    gate, the parts' shares sum to the gated decode over the whole context.  Short contexts
+    leave some parts without keys (their lse is -inf and their share zero)."""
+    from myvllm_b200.ops.full_attention import merge_attention_parts, paged_flash_attention_decode_part
+
+    kc, vc, bt = _paged(ctx_lens, 2, 256, 256, seed=21, device=dev)
+    g = torch.Generator(device=dev).manual_seed(22)
+    q = torch.randn(len(ctx_lens), 16, 256, generator=g, device=dev).to(torch.bfloat16)
+    qg = torch.randn(len(ctx_lens), 16, 512, generator=g, device=dev).to(torch.bfloat16)
+    gate = qg[..., 256:]
+    ctx = torch.tensor(ctx_lens, dtype=torch.int32, device=dev)
+    parts = [paged_flash_attention_decode_part(q, kc, vc, bt.to(dev), ctx, 1 / 16, 256, p, n_parts)
+             for p in range(n_parts)]
+    lse_all = torch.stack([lse for _, lse in parts])
+    assert torch.isfinite(lse_all).any(0).all(), "every (sequence, head) has keys in some part"
+    total = sum(merge_attention_parts(o_p, lse_all, p, output_gate=gate).float() for p, (o_p, _) in enumerate(parts))
+    full = paged_flash_attention_decode(q, kc, vc, bt.to(dev), ctx, 1 / 16, 256, output_gate=gate)
+    assert_close(total, full.float(), what=f"{n_parts} context parts")
+    if len(ctx_lens) == 2:  # the 1-token context lies in part 0 only
+        assert torch.isneginf(lse_all[1:, 0]).all()
