@@ -13,7 +13,10 @@
 // tokens of a tile and runs QK^T and PV on mma.sync m16n8k16 (G padded to 16 rows;
 // the padded rows are never written).  Long contexts are split across CTAs
 // (flash-decoding); split results (normalised O and log2-sum-exp) go to the caller's
-// workspace and a second kernel merges them.
+// workspace and a second kernel merges them.  With long splits, a one-block kernel first
+// orders the split work largest first (every full split, then the partial last splits by
+// length), so that the last wave of CTAs holds the shortest items instead of whatever the
+// grid order left there.
 #include <mutex>
 
 #include "common.cuh"
@@ -35,6 +38,11 @@ struct DecodeParams {
   // o_part [S, Hq, Dv] fp32 with its log2-sum-exp in lse_part [S, Hq].  n_parts == 1: off.
   int part, n_parts;
   float *o_part, *lse_part;
+  // Largest-first order of the split work (null: grid order), int32 [2 S + 2]: [0, S] the
+  // prefix sums of each sequence's full splits run by this call; [S + 1, S + 1 + n) the n
+  // sequences whose partial last split this call runs, longest first; [2 S + 1] n.
+  const int* order;
+  int n_seqs;
   int64_t sq_s, sq_h, so_s, so_h;
   int64_t skc_b, skc_t, skc_h, svc_b, svc_t, svc_h;
   int64_t sbt_s, sbt_b;
@@ -48,6 +56,7 @@ constexpr int kTile = 64;
 constexpr int kWarps = 4;
 
 constexpr int kMaxSplitPages = 1024;  // block-table entries of one split cached in smem
+constexpr int kMaxOrderedSeqs = 4096;  // larger batches run their splits in grid order
 
 template <int D>
 struct DecodeSmem {
@@ -117,6 +126,99 @@ __device__ __forceinline__ void load_tile(const DecodeParams& p, char* sK, char*
   }
 }
 
+// Item i of the largest-first order -> (seq, split); false past the last item.  Items are
+// every sequence's full splits (prefix sums in order[0..S]), then the partial last splits
+// longest first (sequence ids in order[S+1..]).
+__device__ __forceinline__ bool ordered_item(const DecodeParams& p, int i, int& seq, int& split) {
+  const int S = p.n_seqs;
+  const int n_full = p.order[S];
+  if (i < n_full) {
+    int lo = 0, hi = S - 1;  // the last s with order[s] <= i
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.order[mid] <= i) lo = mid;
+      else hi = mid - 1;
+    }
+    seq = lo;
+    split = p.part + (i - p.order[lo]) * p.n_parts;
+    return true;
+  }
+  const int k = i - n_full;
+  if (k >= p.order[2 * S + 1]) return false;
+  seq = p.order[S + 1 + k];
+  split = min(p.ctx[seq], p.n_splits * p.split_len) / p.split_len;
+  return true;
+}
+
+// One block: the largest-first order of a decode call's split work (see DecodeParams).
+// Split j of sequence s is full when (j + 1) L <= ctx_s and partial when j L < ctx_s <
+// (j + 1) L; this call runs the splits with j % n_parts == part.
+__global__ void __launch_bounds__(256) decode_order_kernel(DecodeParams p, int* order) {
+  __shared__ int s_warp[32];
+  __shared__ int s_np;
+  __shared__ int s_key[kMaxOrderedSeqs];
+  const int S = p.n_seqs, L = p.split_len, tid = threadIdx.x;
+  // full splits of this part, per sequence, and an exclusive prefix sum over them
+  int carry = 0;
+  for (int base = 0; base < S; base += blockDim.x) {
+    const int s = base + tid;
+    int f = 0;
+    if (s < S) {
+      const int fa = min(p.ctx[s], p.n_splits * L) / L;  // (a context never exceeds the bound)
+      f = fa > p.part ? (fa - p.part + p.n_parts - 1) / p.n_parts : 0;
+    }
+    int x = f;  // inclusive scan over the block
+    const int lane = tid & 31, w = tid >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int v = lane < (int)(blockDim.x >> 5) ? s_warp[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      s_warp[lane] = v;
+    }
+    __syncthreads();
+    const int incl = x + (w > 0 ? s_warp[w - 1] : 0) + carry;
+    if (s < S) order[s] = incl - f;
+    carry += s_warp[(blockDim.x >> 5) - 1];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    order[S] = carry;
+    s_np = 0;
+  }
+  // partial last splits run by this part, ranked longest first (ties: lower sequence first);
+  // keys in shared memory (the partial's length, -1 where this part runs none)
+  for (int s = tid; s < S; s += blockDim.x) {
+    const int c = min(p.ctx[s], p.n_splits * L), r = c % L, j = c / L;
+    s_key[s] = (r == 0 || j % p.n_parts != p.part) ? -1 : r;
+  }
+  __syncthreads();
+  int np = 0;
+  for (int s = tid; s < S; s += blockDim.x) {
+    const int r = s_key[s];
+    if (r < 0) continue;
+    int rank = 0;
+    for (int t = 0; t < S; ++t) {
+      const int rt = s_key[t];
+      rank += (rt > r) || (rt == r && t < s);
+    }
+    order[S + 1 + rank] = s;
+    ++np;
+  }
+  if (np > 0) atomicAdd(&s_np, np);
+  __syncthreads();
+  if (tid == 0) order[2 * S + 1] = s_np;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams p) {
   using SM = DecodeSmem<D>;
@@ -124,7 +226,14 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(DecodeParams 
   extern __shared__ __align__(128) char smem[];
   char* sQ = smem + NS * SM::kStageBytes;
   int* spages = reinterpret_cast<int*>(sQ + SM::kQBytes);
-  const int split = blockIdx.x * p.n_parts + p.part, kvh = blockIdx.y, seq = blockIdx.z;
+  int split, kvh, seq;
+  if (p.order == nullptr) {
+    split = blockIdx.x * p.n_parts + p.part, kvh = blockIdx.y, seq = blockIdx.z;
+  } else if (!ordered_item(p, blockIdx.y, seq, split)) {
+    return;  // past the last item: no work (the merge skips splits past a context)
+  } else {
+    kvh = blockIdx.x;
+  }
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ctx = p.ctx[seq];
   const int t_begin = split * p.split_len;
@@ -324,12 +433,19 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeParams p)
   const int n_own = p.part < p.n_splits ? (p.n_splits - p.part + p.n_parts - 1) / p.n_parts : 0;
   __shared__ float s_w[1024];
   __shared__ float s_tot;
+  // splits that start past the context hold no keys (and, in largest-first order, no
+  // partial was written for them)
+  const int ctx = p.ctx[seq];
+  auto lse_of = [&](int i) {
+    const int sp = p.part + i * p.n_parts;
+    return sp * p.split_len < ctx ? p.part_lse[(base + sp) * 16 + r] : -INFINITY;
+  };
   float M = -INFINITY;
 #pragma unroll 8
-  for (int i = 0; i < n_own; ++i) M = fmaxf(M, p.part_lse[(base + p.part + i * p.n_parts) * 16 + r]);
+  for (int i = 0; i < n_own; ++i) M = fmaxf(M, lse_of(i));
   float tot = 0.f;
   for (int i = threadIdx.x; i < n_own; i += blockDim.x) {
-    const float l = p.part_lse[(base + p.part + i * p.n_parts) * 16 + r];
+    const float l = lse_of(i);
     const float w = l == -INFINITY ? 0.f : exp2f(l - M);
     s_w[i] = w;
   }
@@ -418,6 +534,14 @@ size_t decode_workspace_bytes(int64_t n_seqs, int64_t hkv, int64_t dv, int n_spl
   return (size_t)n_seqs * hkv * n_splits * 16 * (dv + 1) * sizeof(float);
 }
 
+// The largest-first order table after the split partials (int32 [2 S + 2], 16-byte padded).
+// A call whose workspace lacks this room runs the splits in grid order.
+size_t decode_order_bytes(int64_t n_seqs) { return (size_t)((2 * n_seqs + 2) * 4 + 15) / 16 * 16; }
+size_t decode_workspace_bytes_ordered(int64_t n_seqs, int64_t hkv, int64_t dv, int n_splits, bool parts = false) {
+  const size_t b = decode_workspace_bytes(n_seqs, hkv, dv, n_splits, parts);
+  return b == 0 || n_seqs > kMaxOrderedSeqs ? b : b + decode_order_bytes(n_seqs);
+}
+
 namespace {
 // Internal linkage on purpose: a function-local static of a template with external linkage
 // is a unique symbol that the dynamic loader merges across every loaded copy of the
@@ -428,7 +552,11 @@ int launch_decode(DecodeParams& p, int64_t n_seqs, cudaStream_t st) {
   static unsigned long long attr_mask = 0;
   ensure_smem_attr(paged_decode_kernel<T, D>, smem, attr_mask);
   const int n_own = p.part < p.n_splits ? (p.n_splits - p.part + p.n_parts - 1) / p.n_parts : 0;
-  if (n_own > 0) {
+  if (n_own > 0 && p.order != nullptr) {  // largest-first: (kv head, item), items ordered on device
+    decode_order_kernel<<<1, 256, 0, st>>>(p, const_cast<int*>(p.order));
+    dim3 grid(p.hkv, (unsigned)(n_seqs * n_own));
+    paged_decode_kernel<T, D><<<grid, kWarps * 32, smem, st>>>(p);
+  } else if (n_own > 0) {
     dim3 grid(n_own, p.hkv, (unsigned)n_seqs);
     paged_decode_kernel<T, D><<<grid, kWarps * 32, smem, st>>>(p);
   }
@@ -523,6 +651,17 @@ int run_paged_decode(const char* op, const mvb_tensor* q, const mvb_tensor* kc, 
   p.n_parts = parts ? n_parts : 1;
   p.o_part = parts ? static_cast<float*>(o->data) : nullptr;
   p.lse_part = parts ? static_cast<float*>(lse_part->data) : nullptr;
+  p.n_seqs = (int)S;
+  p.order = nullptr;
+  // Largest-first order when the splits are long enough for the tail of the last wave to
+  // outweigh the extra launch.  Config 4 steps, same box: 2.6% faster with 6.6K-token
+  // splits (TP 1), 1.9% with 3.3K (TP 2), 0.8% slower with 1.7K (TP 4, context split).
+  if (p.part_o != nullptr && S <= kMaxOrderedSeqs && split >= 2048) {
+    const size_t pb = decode_workspace_bytes(S, hkv, dv, n_splits, parts);
+    const int64_t n_own = (n_splits - p.part + p.n_parts - 1) / p.n_parts;
+    if (ws_bytes >= pb + decode_order_bytes(S) && S * n_own <= 65535)
+      p.order = reinterpret_cast<const int*>(static_cast<char*>(ws) + pb);
+  }
 
   if (q->dtype == MVB_BF16) {
     switch (d) {
@@ -550,7 +689,7 @@ extern "C" size_t mvb_paged_attention_decode_workspace_size(int64_t n_seqs, int6
   if (n_seqs <= 0 || hkv <= 0 || max_context_len <= 0) return 0;
   const int split = mvb::decode_split_len(n_seqs, hkv, max_context_len, mvb::kMaxSplits);
   const int n_splits = (int)((max_context_len + split - 1) / split);
-  return mvb::decode_workspace_bytes(n_seqs, hkv, head_v_dim, n_splits);
+  return mvb::decode_workspace_bytes_ordered(n_seqs, hkv, head_v_dim, n_splits);
 }
 
 extern "C" int mvb_paged_attention_decode(const mvb_tensor* q, const mvb_tensor* k_cache, const mvb_tensor* v_cache,
@@ -582,7 +721,7 @@ extern "C" size_t mvb_paged_attention_decode_part_workspace_size(int64_t n_seqs,
   if (n_seqs <= 0 || num_kv_heads <= 0 || max_context_len <= 0 || n_parts < 1) return 0;
   const int split = mvb::decode_split_len(n_seqs, num_kv_heads, max_context_len, mvb::kMaxSplits, n_parts);
   const int n_splits = (int)((max_context_len + split - 1) / split);
-  return mvb::decode_workspace_bytes(n_seqs, num_kv_heads, head_v_dim, n_splits, true);
+  return mvb::decode_workspace_bytes_ordered(n_seqs, num_kv_heads, head_v_dim, n_splits, true);
 }
 
 extern "C" int mvb_paged_attention_decode_part(const mvb_tensor* q, const mvb_tensor* k_cache,

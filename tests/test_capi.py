@@ -141,8 +141,11 @@ def test_decode_workspace_size_policy():
     small = lib.mvb_paged_attention_decode_workspace_size(128, 2, 256, 512)
     big = lib.mvb_paged_attention_decode_workspace_size(128, 2, 256, 32768)
     assert big >= small
-    # split results: [S, Hkv, splits, 16, Dv + 1] fp32
-    assert big % (128 * 2 * 16 * 257 * 4) == 0
+    # split results [S, Hkv, splits, 16, Dv + 1] fp32, then the largest-first order table
+    # int32 [2 S + 2] padded to 16 bytes
+    order = (2 * 128 + 2) * 4 // 16 * 16 + (16 if (2 * 128 + 2) * 4 % 16 else 0)
+    assert (big - order) % (128 * 2 * 16 * 257 * 4) == 0
+    assert lib.mvb_paged_attention_decode_part_workspace_size(128, 1, 256, 32768, 2) > 0
 
 
 def test_ops_refuse_cpu_tensors():

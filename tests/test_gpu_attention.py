@@ -256,3 +256,38 @@ def test_paged_decode_context_parts(n_parts, ctx_lens):
     assert_close(total, full.float(), what=f"{n_parts} context parts")
     if len(ctx_lens) == 2:  # the 1-token context lies in part 0 only
         assert torch.isneginf(lse_all[1:, 0]).all()
+
+
+def test_paged_decode_largest_first_order_is_bit_identical():
+    """With long splits the decode orders its split work largest first (a one-block kernel
+    builds the order in the workspace); the partials and their merge are the same as in grid
+    order, so the output is bit-identical to a call whose workspace has no room for the
+    order table.  Contexts include exact multiples of the split length (no partial split),
+    a single token and a split plus one token."""
+    from myvllm_b200 import _lib
+
+    split = 6592  # the policy's split for 128 sequences x 2 kv heads and a 32768 bound
+    ctx = W.seq_lengths(128, 1024, 32768, 4)
+    ctx[:6] = [split, 2 * split, 1, split + 1, 32768, 64]
+    kc, vc, bt = _paged(ctx, 2, 256, 256, seed=31, extra_blocks=0, device=dev)
+    q = torch.randn(128, 16, 256, generator=torch.Generator().manual_seed(32)).to(torch.bfloat16).to(dev)
+    bt, cl = bt.to(dev), torch.tensor(ctx, dtype=torch.int32, device=dev)
+    full = _lib.load().mvb_paged_attention_decode_workspace_size(128, 2, 256, 32768)
+    partials = 128 * 2 * 5 * 16 * 257 * 4
+    assert full > partials
+    outs = []
+    for nbytes in (full, partials):
+        ws = torch.zeros(full, dtype=torch.uint8, device=dev)
+        o = torch.empty(128, 16, 256, dtype=torch.bfloat16, device=dev)
+        _lib.call("decode", "mvb_paged_attention_decode", _lib.desc(q), _lib.desc(kc), _lib.desc(vc), _lib.desc(bt),
+                  _lib.desc(cl), 1 / 16, 256, 32768, _lib.desc(o), ws.data_ptr(), nbytes, _lib.stream_of(q))
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    for s in range(6):
+        n = ctx[s]
+        blocks = bt[s, torch.arange(n, device=dev) // 256].long()
+        kk = kc[blocks, torch.arange(n, device=dev) % 256].float()
+        vv = vc[blocks, torch.arange(n, device=dev) % 256].float()
+        p = torch.softmax(torch.einsum("hgd,nhd->hgn", q[s].float().view(2, 8, 256), kk) / 16, -1)
+        assert_close(outs[0][s], torch.einsum("hgn,nhd->hgd", p, vv).reshape(16, 256), what=f"seq {s}")
