@@ -97,14 +97,26 @@ int mvb_causal_conv1d_update(const mvb_tensor* x, const mvb_tensor* weight, mvb_
  * final state; cu_seqlens [S+1]; o [T, Hv, V] (dtype of v).  scale <= 0 means K^-0.5.
  * use_qk_l2norm != 0 applies the layer's q/k L2 normalisation (x * rsqrt(sum x^2 + 1e-6),
  * m/layers/linear_attention.py:113-114) inside the kernel.
- * workspace: NULL, or >= 8 bytes of zero-initialised device memory used as a work counter
- * (sequences are then scheduled dynamically, longest first); the kernel leaves it zeroed.
+ * workspace: NULL, or zero-initialised device memory that the kernel keeps ready for the
+ * next launch:
+ *   >= mvb_chunk_gated_delta_rule_workspace_size() bytes: the (sequence, v-head) chains are
+ *      balanced over the SMs.  Laid end to end, they are cut into one equal span per SM;
+ *      a chain cut at a span boundary runs its first part on one SM and its rest on the
+ *      next, the state passing through recurrent_state under a flag in the workspace
+ *      (cooperative launch; results are bit-identical to whole-chain scheduling);
+ *   8 bytes up to that: a work counter, whole chains scheduled dynamically, longest first;
+ *   NULL: whole chains round-robin.
  * Launches that share one workspace must be ordered (same stream). */
 int mvb_chunk_gated_delta_rule(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                                const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,
                                const mvb_tensor* recurrent_state_indices, const mvb_tensor* cu_seqlens,
                                mvb_tensor* o, float scale, int use_qk_l2norm, void* workspace,
                                size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace the chunked gated delta rule entry points need on the current device
+ * for the balanced schedule (a few hundred bytes; no counterpart in the reference, whose
+ * chunk pipeline loops over chunks on the host, m/ops/gated_delta_rule/h.py:195-265). */
+size_t mvb_chunk_gated_delta_rule_workspace_size(void);
 
 /* Recurrent gated delta rule, one token per sequence (decode).  q,k [S, Hk, K];
  * v [S, Hv, V]; g, beta [S, Hv]; state [S_max, Hv, K, V] fp32 updated in place;

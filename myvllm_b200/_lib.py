@@ -56,6 +56,7 @@ SIGNATURES = {
     "mvb_last_error": (ctypes.c_char_p, []),
     "mvb_causal_conv1d_fn": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, ctypes.c_int, _P]),
     "mvb_causal_conv1d_update": (ctypes.c_int, [_T, _T, _T, _T, _T, ctypes.c_int, _P]),
+    "mvb_chunk_gated_delta_rule_workspace_size": (ctypes.c_size_t, []),
     "mvb_chunk_gated_delta_rule": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int,
                                                   _P, ctypes.c_size_t, _P]),
     "mvb_fused_recurrent_gdn": (ctypes.c_int, [_T, _T, _T, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_int, _P]),
@@ -213,6 +214,12 @@ def workspace(device: torch.device, nbytes: int, tag: str = "scratch") -> torch.
         buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf
+
+
+def chunk_gdn_workspace(device: torch.device) -> torch.Tensor:
+    """Zero-initialised workspace of the chunked GDN entry points, sized for the balanced
+    schedule (the chains spread evenly over the SMs, with state hand-offs between them)."""
+    return workspace(device, int(load().mvb_chunk_gated_delta_rule_workspace_size()), tag="gdn_chunk")
 
 
 def device_status() -> int:

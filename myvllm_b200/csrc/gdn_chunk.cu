@@ -26,8 +26,9 @@ bool chunk_tc_supported(const mvb_tensor* q, const mvb_tensor* k, const mvb_tens
                         const mvb_tensor* beta, const mvb_tensor* state, const mvb_tensor* o);
 int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
                     const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
-                    mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, const GateDev& gd,
-                    cudaStream_t st, const NormDev& nd);
+                    mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, size_t work_bytes,
+                    const GateDev& gd, cudaStream_t st, const NormDev& nd);
+size_t chunk_gdn_workspace_bytes(int grid);
 
 int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
               const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
@@ -50,7 +51,8 @@ int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
   if (n_seqs == 0 || v->shape[1] == 0) return MVB_OK;
   MVB_CHECK_ARG(ws == nullptr || (ws_bytes >= 8 && (reinterpret_cast<uintptr_t>(ws) & 3) == 0),
                 "%s: workspace must be at least 8 bytes, 4-byte aligned", op);
-  rc = launch_chunk_tc(q, k, v, g, beta, state, idx, cu, o, scale, l2norm, n_seqs, static_cast<int*>(ws), gd, st, nd);
+  rc = launch_chunk_tc(q, k, v, g, beta, state, idx, cu, o, scale, l2norm, n_seqs, static_cast<int*>(ws), ws_bytes, gd,
+                       st, nd);
   if (rc < 0 && nd.z != nullptr) MVB_FAIL(MVB_ERR_CUDA, "%s: the TMA descriptors of q/k/v could not be built", op);
   if (rc < 0) {
     set_path(MVB_OP_CHUNK_GDN, MVB_PATH_SERIAL, "the TMA descriptors of q/k/v could not be built");
@@ -61,6 +63,10 @@ int run_chunk(const char* op, const mvb_tensor* q, const mvb_tensor* k, const mv
 }
 
 }  // namespace mvb
+
+extern "C" size_t mvb_chunk_gated_delta_rule_workspace_size(void) {
+  return mvb::chunk_gdn_workspace_bytes(mvb::num_sms());
+}
 
 extern "C" int mvb_chunk_gated_delta_rule(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v,
                                           const mvb_tensor* g, const mvb_tensor* beta, mvb_tensor* recurrent_state,

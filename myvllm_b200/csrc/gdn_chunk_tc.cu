@@ -30,10 +30,15 @@
 //                     state copy for chunk c+1.
 // They hand buffers over through mbarriers (normed / factors-ready / gates-ready from prep;
 // MMA completions from rec).  prep publishes chunk c+1 only once the U/W products of chunk
-// c are done, which keeps it at most one phase ahead on every barrier.  Chains are handed out longest sequence first over a
-// persistent grid: dynamically through a work counter when the caller supplies one (the
-// last CTA to run dry zeroes it for the next launch), else round-robin.  Every wait is
-// bounded; a wait that gives up sets the device error word and the CTA winds down.
+// c are done, which keeps it at most one phase ahead on every barrier.
+//
+// Scheduling over the persistent grid (one CTA per SM).  With a full workspace the chains are
+// balanced: laid end to end they are cut into one equal span per CTA pair, a chain cut at a
+// span boundary hands its state to the next pair through recurrent_state and a flag, and the
+// two CTAs of a pair (the two SMs of a TPC) run the two v-heads of one k-head side by side.
+// With an 8-byte workspace whole chains go out longest sequence first through a work
+// counter, without one round-robin.  Every wait is bounded; a wait that gives up sets the
+// device error word and the CTA winds down.
 #include <type_traits>
 
 #include "tcgen05.cuh"
@@ -86,7 +91,10 @@ struct Params {
   const int32_t* state_idx;
   const int32_t* cu;
   int64_t so_t, so_h, sg_t, sg_h, sb_t, sb_h, ss_n, ss_h, ss_k;
-  int* work;  // [next chain, CTAs done] or null
+  // Workspace words: [0] next chain (dynamic schedule), [1] CTAs done, [2] launch
+  // generation, [3 + i] hand-off flag of CTA i (balanced schedule); or null
+  int* work;
+  int balanced;  // 1: balanced spans with state hand-offs (needs work[0 .. 3 + grid))
   int n_seqs, hk, hv, l2norm, g32, b32;
   float scale;
   GateDev gd;  // raw gates (a, b in the g, beta slots) when gd.alog is set
@@ -100,7 +108,9 @@ struct Bars {
 
 // chunk record handed from prep to rec
 struct Rec {
-  int seq, h, c0, n, flags;  // flags: 1 valid, 2 first chunk of its chain, 4 last chunk
+  // flags: 1 valid, 2 first chunk of a segment (load the state), 4 last chunk of a segment
+  // (store the state), 8 wait for the previous CTA's hand-off first, 16 publish a hand-off
+  int seq, h, c0, n, flags;
 };
 
 __device__ __forceinline__ float ldg_f(const void* p, int64_t i, bool f32, bool is_bf16) {
@@ -128,6 +138,25 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Hand-off flags between CTAs (gpu scope): the writer's state stores are fenced before the
+// release store; the reader's acquire load precedes its state loads.
+__device__ __forceinline__ void st_release(int* f, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire(const int* f) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+// Waits (about a second at most) until *f == v; false if it gave up.
+__device__ __forceinline__ bool wait_flag(const int* f, int v) {
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (ld_acquire(f) == v) return true;
+    __nanosleep(256);
+  }
+  return false;
 }
 
 // fp32 -> fp16 hi + lo (x ~ hi + lo to ~2^-22 relative), packed in pairs.
@@ -285,9 +314,10 @@ __device__ __forceinline__ void solve_tril64(char* a_hi, char* a_lo, const float
   }
 }
 
+// One chunk of a segment: a (sequence, v-head) chain, or the part of one that a CTA runs.
 struct Item {
-  int seq, h, c0, n, t_end;
-  bool valid, first;
+  int seq, h, c0, n, t_end;  // t_end: end token of the segment
+  bool valid, first, wait, pub;
 };
 
 template <typename T, bool NORM>
@@ -298,7 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
   __shared__ Rec recs[2];
   __shared__ float s_el[2];  // e^{G_last} of the chunk in each record slot
   __shared__ uint32_t tmem_slot;
-  __shared__ int s_chain;
+  __shared__ int s_seg[5];  // next segment: seq, v-head, first chunk, end chunk, flags (1 valid, 2 wait, 4 publish)
+  __shared__ int s_gen;     // launch generation (balanced schedule)
   __shared__ int s_end;  // set by prep when the work runs out
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -332,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     for (uint64_t* m : {&bars.mma2_go, &bars.normed, &bars.mma_all, &bars.mma_all_prep})
       umma::mbar_init(m, 1);
     s_end = 0;
+    s_gen = p.balanced ? *reinterpret_cast<volatile int*>(p.work + 2) : 0;
     umma::mbar_init(&bars.raw_v, 1);
     umma::mbar_init(&bars.d1_done, 1);
     umma::mbar_init(&bars.mma2_done, 1);
@@ -352,51 +384,184 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     // Per iteration k: mask/solve/factors of chunk k, then (while U/W(k) run on the tensor
     // core) the gates and norms of chunk k+1, then W staging and the hand-over of chunk k.
     const int wg = tid >> 7;  // column half of the TMEM tiles this thread reads
-    auto chain_item = [&](int chain) -> Item {
+    auto seq_at = [&](int r) { return sorted ? (int)sPerm[r] : r; };
+    auto nch = [&](int seq) { return (p.cu[seq + 1] - p.cu[seq] + C - 1) / C; };
+    // thread 0 writes the next segment to s_seg; all prep threads then read it with seg_item
+    auto put = [&](int seq, int h, int cb, int ce, int flags) {
+      s_seg[0] = seq;
+      s_seg[1] = h;
+      s_seg[2] = cb;
+      s_seg[3] = ce;
+      s_seg[4] = flags;
+    };
+    auto seg_item = [&]() -> Item {
       Item it;
-      it.valid = chain < n_chains;
+      it.valid = s_seg[4] & 1;
       it.first = true;
+      it.wait = s_seg[4] & 2;
+      it.pub = s_seg[4] & 4;
       if (!it.valid) return it;
-      it.seq = sorted ? sPerm[chain / p.hv] : chain / p.hv;
-      it.h = chain % p.hv;
-      it.c0 = p.cu[it.seq];
-      it.t_end = p.cu[it.seq + 1];
+      it.seq = s_seg[0];
+      it.h = s_seg[1];
+      const int base = p.cu[it.seq];
+      it.c0 = base + s_seg[2] * C;
+      it.t_end = min(p.cu[it.seq + 1], base + s_seg[3] * C);
       it.n = min(C, it.t_end - it.c0);
       return it;
     };
-    // thread 0: the next non-empty chain for this CTA (>= n_chains when none is left)
-    int rr = 0;
+    // thread 0: out of work -> count this CTA out; the last CTA readies the workspace for the
+    // next launch (dynamic: zero the chain counter; balanced: advance the generation)
     bool exhausted = false;
-    auto fetch = [&]() -> int {
+    auto count_out = [&]() {
+      if (exhausted) return;
+      exhausted = true;
+      if (p.work && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
+        p.work[1] = 0;
+        if (p.balanced) p.work[2] = s_gen + 1;
+        else p.work[0] = 0;
+      }
+    };
+    // Dynamic / round-robin schedule: whole chains, longest sequence first.
+    int rr = 0;
+    auto fetch_dynamic = [&]() {
       for (;;) {
         const int c = p.work ? atomicAdd(p.work, 1) : (int)blockIdx.x + (rr++) * (int)gridDim.x;
         if (c >= n_chains) {
-          exhausted = true;
-          if (p.work && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
-            p.work[0] = 0;
-            p.work[1] = 0;
-          }
-          return c;
+          put(0, 0, 0, 0, 0);
+          count_out();
+          return;
         }
-        if (chain_item(c).n > 0) return c;
+        const int seq = seq_at(c / p.hv), n = nch(seq);
+        if (n > 0) {
+          put(seq, c % p.hv, 0, n, 1);
+          return;
+        }
       }
     };
-    // the item after `it` (fetching a new chain when `it` ends one); all prep threads call it
-    int chain = 0;
+    // Balanced schedule (McNaughton's wrap-around rule, with the order of the two cut
+    // parts chosen for a serial chain): the chains laid end to end in schedule order
+    // (sequences longest first, heads in order) cover ntot chunks; CTA i owns positions
+    // [i cs, (i+1) cs), cs = max(ceil(ntot / grid), longest chain), so the makespan is
+    // about ntot / grid chunks instead of what whole chains allow.  A chain cut at the
+    // span's end (the tail cut) runs FIRST and stores its state for the next CTA; a chain
+    // cut at the span's start (the head cut) runs LAST and first waits for the previous
+    // CTA's hand-off.  The two parts of a chain together are at most cs long, so the first
+    // part is normally done before the second is reached.  Thread 0 only.
+    // CTA pairs (2m, 2m + 1) run the two v-heads of one unit -- (sequence, v-heads 2j and
+    // 2j + 1), which share a k-head -- side by side, cut at the same places: the two SMs of
+    // a TPC then work on the same q/k tiles and the same code in step
+    const int pair = (p.hv % 2 == 0 && gridDim.x % 2 == 0) ? 2 : 1;
+    const int hu = p.hv / pair, ulane = (int)blockIdx.x % pair;  // units per sequence; v-head in the unit
+    int ph = 3, br = 0, bh = 0;           // phase; next whole unit (rank, unit head)
+    long long bpos = 0, bend = 0;         // its start position; end of the whole chains
+    int t_seq = -1, t_h = 0, t_len = 0;   // tail cut: chunks [0, t_len)
+    int h_seq = -1, h_h = 0, h_off = 0;   // head cut: chunks [h_off, end)
+    if (p.balanced && tid == 0) {
+      long long ntot = 0;
+      int maxn = 0;
+      for (int sq = 0; sq < S; ++sq) {
+        const int n = nch(sq);
+        ntot += (long long)n * hu;
+        maxn = max(maxn, n);
+      }
+      const long long nm = gridDim.x / pair;
+      const long long cs = max((ntot + nm - 1) / nm, (long long)maxn);
+      const long long A = (long long)(blockIdx.x / pair) * cs, B = min(A + cs, ntot);
+      // the chain that covers position pos: rank r, head h, its start position
+      auto locate = [&](long long pos, int& r, int& h, long long& start) {
+        long long P = 0;
+        for (r = 0; r < S; ++r) {
+          const long long w = (long long)nch(seq_at(r)) * hu;
+          if (P + w > pos) break;
+          P += w;
+        }
+        const int n = nch(seq_at(r));
+        h = (int)((pos - P) / n);
+        start = P + (long long)h * n;
+      };
+      if (A < B) {
+        ph = 0;
+        long long sa;
+        locate(A, br, bh, sa);
+        bpos = sa;
+        if (sa < A) {
+          h_seq = seq_at(br);
+          h_h = bh * pair + ulane;
+          h_off = (int)(A - sa);
+          bpos = sa + nch(h_seq);
+          if (++bh == hu) {
+            bh = 0;
+            ++br;
+          }
+        }
+        bend = B;
+        if (B < ntot) {
+          int rb, hb;
+          long long sb;
+          locate(B, rb, hb, sb);
+          if (sb < B) {
+            t_seq = seq_at(rb);
+            t_h = hb * pair + ulane;
+            t_len = (int)(B - sb);
+            bend = sb;
+          }
+        }
+      }
+    }
+    auto fetch_balanced = [&]() {
+      if (ph == 0) {
+        ph = 1;
+        if (t_seq >= 0) {
+          put(t_seq, t_h, 0, t_len, 1 | 4);
+          return;
+        }
+      }
+      if (ph == 1) {
+        while (br < S && nch(seq_at(br)) == 0) {
+          ++br;
+          bh = 0;
+        }
+        if (br < S && bpos < bend) {
+          const int sq = seq_at(br), n = nch(sq);
+          put(sq, bh * pair + ulane, 0, n, 1);
+          bpos += n;
+          if (++bh == hu) {
+            bh = 0;
+            ++br;
+          }
+          return;
+        }
+        ph = 2;
+      }
+      if (ph == 2) {
+        ph = 3;
+        if (h_seq >= 0) {
+          put(h_seq, h_h, h_off, nch(h_seq), 1 | 2);
+          return;
+        }
+      }
+      put(0, 0, 0, 0, 0);
+      count_out();
+    };
+    auto fetch = [&]() {
+      if (p.balanced) fetch_balanced();
+      else fetch_dynamic();
+    };
+    // the item after `it` (fetching the next segment when `it` ends one); all prep threads call it
     auto next_item = [&](const Item& it) -> Item {
       if (!it.valid) return it;
       Item nx = it;
-      if (it.c0 + C < it.t_end) {  // same chain (uniform across the group: no barrier needed)
+      if (it.c0 + C < it.t_end) {  // same segment (uniform across the group: no barrier needed)
         nx.c0 += C;
         nx.n = min(C, nx.t_end - nx.c0);
         nx.first = false;
+        nx.wait = false;
         return nx;
       }
-      if (tid == 0) s_chain = fetch();
+      if (tid == 0) fetch();
       bar_sync(kBarPrep, kPrep);
-      chain = s_chain;
-      nx = chain_item(chain);
-      bar_sync(kBarPrep, kPrep);  // s_chain may be rewritten by the next call
+      nx = seg_item();
+      bar_sync(kBarPrep, kPrep);  // s_seg may be rewritten by the next call
       return nx;
     };
     // loads issued / consumed (thread 0), for the drain on exit
@@ -517,17 +682,17 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
         r.h = it.h;
         r.c0 = it.c0;
         r.n = it.n;
-        r.flags = 1 | (it.first ? 2 : 0) | (it.c0 + C >= it.t_end ? 4 : 0);
+        const bool last = it.c0 + C >= it.t_end;
+        r.flags = 1 | (it.first ? 2 : 0) | (last ? 4 : 0) | (it.first && it.wait ? 8 : 0) | (last && it.pub ? 16 : 0);
         recs[kk & 1] = r;
         tma::arrive(&bars.normed);
       }
       return true;
     };
 
-    if (tid == 0) s_chain = fetch();
+    if (tid == 0) fetch();
     bar_sync(kBarPrep, kPrep);
-    chain = s_chain;
-    Item cur = chain_item(chain);
+    Item cur = seg_item();
     bar_sync(kBarPrep, kPrep);
     Item nxt = next_item(cur);
     if (tid == 0 && cur.valid) {
@@ -699,11 +864,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       umma::mbar_wait(&bars.mma_all_prep, 0);
       for (int i = qk_used; i < qk_issued; ++i) umma::mbar_wait(&bars.raw_qk[i & 1], (i >> 1) & 1);
       for (int i = v_used; i < v_issued; ++i) umma::mbar_wait(&bars.raw_v, i & 1);
-      // an aborted CTA still counts itself out so the work counter is zeroed for the next launch
-      if (p.work && !exhausted && atomicAdd(p.work + 1, 1) == (int)gridDim.x - 1) {
-        p.work[0] = 0;
-        p.work[1] = 0;
-      }
+      // an aborted CTA still counts itself out so the workspace is readied for the next launch
+      count_out();
     }
   } else {
     // ================================================================ rec group
@@ -858,8 +1020,15 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       umma::fence_before();
       bar_sync(kBarRec, kRec);
 
-      // ---- chain start: state -> TMEM (pre-scaled by e^{G_last}) and its fp16 copy ----
+      // ---- segment start: state -> TMEM (pre-scaled by e^{G_last}) and its fp16 copy; a
+      //      head cut first waits for the previous CTA to hand the state over ----
       if (rec.flags & 2) {
+        if (rec.flags & 8) {
+          // the unit's previous part ran on the same lane of the previous CTA pair
+          const int pair = (p.hv % 2 == 0 && gridDim.x % 2 == 0) ? 2 : 1;
+          if (rt == 0) ok = wait_flag(p.work + 3 + blockIdx.x - pair, s_gen + 1);
+          if (!(ok = bar_and(kBarRec, kRec, ok))) break;
+        }
         gstate = p.state + (int64_t)p.state_idx[rec.seq] * p.ss_n + (int64_t)rec.h * p.ss_h;
         const float el = s_el[b];
         const float* srow = gstate + (int64_t)tl * p.ss_k;
@@ -868,7 +1037,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
           float v[16];
 #pragma unroll
           for (int j = 0; j < 16; j += 4) {
-            const float4 x = *reinterpret_cast<const float4*>(srow + cc + j);
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(srow + cc + j));  // L2: may be a hand-off
             v[j] = x.x; v[j + 1] = x.y; v[j + 2] = x.z; v[j + 3] = x.w;
           }
 #pragma unroll
@@ -956,6 +1125,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
           for (int j = 0; j < 16; j += 4)
             *reinterpret_cast<float4*>(srow + cc + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         }
+        if (rec.flags & 16) __threadfence();  // the hand-off: state stores before the flag
       } else {
         const int nb = (k + 1) & 1;
         ok = umma::mbar_wait(&bars.gready[nb], ((k + 1) >> 1) & 1);
@@ -982,6 +1152,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       umma::fence_async_smem();
       umma::fence_before();
       if (!(ok = bar_and(kBarRec, kRec, ok))) break;
+      if ((rec.flags & 16) && rt == 0) st_release(p.work + 3 + blockIdx.x, s_gen + 1);
       // the tile goes to HBM in the next chunk's U/W window (SM_O is next written by its Vn
       // staging, which follows the hand-over of that chunk)
       pend_c0 = rec.c0;
@@ -1027,12 +1198,16 @@ bool chunk_tc_supported(const mvb_tensor* q, const mvb_tensor* k, const mvb_tens
          (beta->dtype == MVB_F32 || beta->dtype == q->dtype);
 }
 
+// Workspace of the balanced schedule for a grid of `grid` CTAs: the dynamic chain counter,
+// the done counter, the launch generation and one hand-off flag per CTA (int32 words).
+size_t chunk_gdn_workspace_bytes(int grid) { return sizeof(int) * (3 + (size_t)grid); }
+
 // Returns -1 when the TMA descriptors cannot be built (the caller then runs the token-serial
 // kernel), else an MVB status.
 int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* v, const mvb_tensor* g,
                     const mvb_tensor* beta, mvb_tensor* state, const mvb_tensor* idx, const mvb_tensor* cu,
-                    mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, const GateDev& gd,
-                    cudaStream_t st, const NormDev& nd) {
+                    mvb_tensor* o, float scale, int l2norm, int64_t n_seqs, int* work, size_t work_bytes,
+                    const GateDev& gd, cudaStream_t st, const NormDev& nd) {
   Params p;
   memset(&p, 0, sizeof(p));
   const int64_t T_tok = q->shape[0];
@@ -1058,28 +1233,33 @@ int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* 
   p.nd = nd;
   const int chains = (int)(n_seqs * p.hv);
   const int grid = chains < num_sms() ? chains : num_sms();
+  // the balanced schedule has CTAs wait for each other's hand-offs: a cooperative launch
+  // guarantees that the whole grid (one CTA per SM) is resident at once
+  p.balanced = work != nullptr && work_bytes >= chunk_gdn_workspace_bytes(grid) ? 1 : 0;
   const bool norm = nd.z != nullptr;
-  if (q->dtype == MVB_BF16) {
-    if (norm) {
-      static unsigned long long attr_mask = 0;
-      ensure_smem_attr(gdn_chunk_tc_kernel<__nv_bfloat16, true>, SMEM_BYTES, attr_mask);
-      gdn_chunk_tc_kernel<__nv_bfloat16, true><<<grid, kThreads, SMEM_BYTES, st>>>(p);
-    } else {
-      static unsigned long long attr_mask = 0;
-      ensure_smem_attr(gdn_chunk_tc_kernel<__nv_bfloat16, false>, SMEM_BYTES, attr_mask);
-      gdn_chunk_tc_kernel<__nv_bfloat16, false><<<grid, kThreads, SMEM_BYTES, st>>>(p);
-    }
-  } else {
-    if (norm) {
-      static unsigned long long attr_mask = 0;
-      ensure_smem_attr(gdn_chunk_tc_kernel<__half, true>, SMEM_BYTES, attr_mask);
-      gdn_chunk_tc_kernel<__half, true><<<grid, kThreads, SMEM_BYTES, st>>>(p);
-    } else {
-      static unsigned long long attr_mask = 0;
-      ensure_smem_attr(gdn_chunk_tc_kernel<__half, false>, SMEM_BYTES, attr_mask);
-      gdn_chunk_tc_kernel<__half, false><<<grid, kThreads, SMEM_BYTES, st>>>(p);
-    }
-  }
+  // the four kernels share one function-pointer type: each keeps its own attribute mask
+  static unsigned long long mask_bf = 0, mask_bf_norm = 0, mask_h = 0, mask_h_norm = 0;
+  auto go = [&](auto kernel, unsigned long long& attr_mask) -> cudaError_t {
+    ensure_smem_attr(kernel, SMEM_BYTES, attr_mask);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.balanced ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+  };
+  cudaError_t e;
+  if (q->dtype == MVB_BF16)
+    e = norm ? go(gdn_chunk_tc_kernel<__nv_bfloat16, true>, mask_bf_norm)
+             : go(gdn_chunk_tc_kernel<__nv_bfloat16, false>, mask_bf);
+  else
+    e = norm ? go(gdn_chunk_tc_kernel<__half, true>, mask_h_norm) : go(gdn_chunk_tc_kernel<__half, false>, mask_h);
+  if (e != cudaSuccess) MVB_FAIL(MVB_ERR_CUDA, "chunk_gated_delta_rule: launch failed: %s", cudaGetErrorString(e));
   MVB_CHECK_LAUNCH("chunk_gated_delta_rule");
   return MVB_OK;
 }

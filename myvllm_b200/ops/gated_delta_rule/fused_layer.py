@@ -79,7 +79,7 @@ def gated_deltanet_prefill(q, k, v, a, b, A_log, dt_bias, recurrent_state, recur
     idx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
     cu = cu_seqlens if cu_seqlens.dtype == torch.int32 else cu_seqlens.int()
     out = torch.empty(v.shape, dtype=v.dtype, device=v.device)
-    ws = _lib.workspace(q.device, 8, tag="gdn_chunk")  # work counter of the dynamic scheduler
+    ws = _lib.chunk_gdn_workspace(q.device)
     _lib.call("gated_deltanet_prefill", "mvb_gated_deltanet_prefill", _lib.desc(q), _lib.desc(k), _lib.desc(v),
               _lib.desc(a), _lib.desc(b), _lib.desc(A_log), _lib.desc(dt_bias), _lib.desc(recurrent_state),
               _lib.desc(idx), _lib.desc(cu), _lib.desc(z), _lib.desc(norm_weight), float(norm_eps), _lib.desc(out),

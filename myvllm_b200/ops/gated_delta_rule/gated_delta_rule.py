@@ -51,7 +51,7 @@ def chunk_gated_delta_rule(
     idx = recurrent_state_indices if recurrent_state_indices.dtype == torch.int32 else recurrent_state_indices.int()
     cu = cu_seqlens if cu_seqlens.dtype == torch.int32 else cu_seqlens.int()
     o = torch.empty(v.shape, dtype=v.dtype, device=v.device)
-    ws = _lib.workspace(q.device, 8, tag="gdn_chunk")  # work counter of the dynamic scheduler
+    ws = _lib.chunk_gdn_workspace(q.device)
     scale = float(k.shape[-1] ** -0.5)
     if gate_inputs is not None:
         if g is not None or beta is not None:

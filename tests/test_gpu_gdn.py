@@ -119,6 +119,49 @@ def test_chunk_c1_shapes_vs_fp32_recurrent_kernel():
     assert_state_close(a["state"], b["state"])
 
 
+def _chunk_call(d, o, ws):
+    from myvllm_b200 import _lib
+
+    _lib.call("chunk_gated_delta_rule", "mvb_chunk_gated_delta_rule", _lib.desc(d["q"]), _lib.desc(d["k"]),
+              _lib.desc(d["v"]), _lib.desc(d["g"]), _lib.desc(d["beta"]), _lib.desc(d["state"]), _lib.desc(d["idx"]),
+              _lib.desc(d["cu"]), _lib.desc(o), 0.0, 0, ws.data_ptr() if ws is not None else None,
+              ws.numel() if ws is not None else 0, _lib.stream_of(d["q"]))
+
+
+def test_chunk_balanced_schedule_is_bit_identical_to_whole_chains():
+    """The balanced schedule cuts (sequence, v-head) chains at SM span boundaries and hands
+    the state over through recurrent_state (28 cuts for these lengths at 32 v-heads).  The
+    fp32 state passes through memory exactly, so outputs and final states must equal those
+    of whole-chain scheduling (the 8-byte dynamic counter, and round-robin without a
+    workspace) bit for bit, on two balanced launches in a row (the launch generation
+    advances between them)."""
+    from myvllm_b200 import _lib
+
+    cpu = _rand_gdn([1000, 700, 300], 16, 32, 128, 128, seed=21, n_slots=6)
+    base = _to(cpu, dev)
+    ws_bal = torch.zeros(int(_lib.load().mvb_chunk_gated_delta_rule_workspace_size()), dtype=torch.uint8, device=dev)
+    ws_dyn = torch.zeros(8, dtype=torch.uint8, device=dev)
+    outs = {}
+    for name, ws in (("balanced", ws_bal), ("balanced again", ws_bal), ("dynamic", ws_dyn), ("round-robin", None)):
+        d = dict(base, state=base["state"].clone())
+        o = torch.empty_like(d["v"])
+        _chunk_call(d, o, ws)
+        torch.cuda.synchronize()
+        assert _lib.device_status() == 0, name
+        outs[name] = (o, d["state"])
+    ref_o, ref_s = outs["dynamic"]
+    for name, (o, s) in outs.items():
+        assert torch.equal(o, ref_o), f"o differs: {name} vs dynamic"
+        assert torch.equal(s, ref_s), f"state differs: {name} vs dynamic"
+    st = cpu["state"].double().numpy()
+    ref = oracle.gdn.chunked(to_np(cpu["q"]), to_np(cpu["k"]), to_np(cpu["v"]), to_np(cpu["g"]), to_np(cpu["beta"]),
+                             st, cpu["idx"].numpy(), cpu["cu"].numpy(), 64)
+    assert_close(outs["balanced"][0], ref, what="o (balanced schedule vs oracle)")
+    assert_state_close(outs["balanced"][1], st, what="state (balanced schedule vs oracle)")
+    words = ws_bal.view(torch.int32)
+    assert words[1].item() == 0 and words[2].item() == 2, "done counter / launch generation"
+
+
 def test_chunk_tc_full_c1_sequence_vs_oracle():
     """One full-length config-1 sequence (8192 tokens) through the tensor-core chunk kernel
     against the oracle (m/ops/gated_delta_rule/gated_delta_rule.py:44-64, restated in
