@@ -10,14 +10,17 @@
 //              ring (by head dim 256, 128, 64), K_j issued ahead of V_{j-1}
 //              (3-D maps [T, H, D] for contiguous K/V; 4-D maps [blocks, bs, H, D] for the
 //              paged cache, one box per page segment);
-//   warp 1     MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score buffers,
-//              then O += P_{j-1} V_{j-1} into the TMEM output accumulator, so the tensor
-//              core computes the next scores while the softmax warps work on this tile;
-//   warps 2-5  softmax: one query row per thread (TMEM lane = row), P written to shared
-//              memory in the 128-byte-swizzled K-major layout the PV MMA reads; the output
-//              is rescaled only when a row maximum grows by more than 2^8 (the final 1/l
+//   warp 1     MMA issuer (one thread): S_j = Q K_j^T into a TMEM score buffer, then
+//              O += P_{j-1} V_{j-1} into the TMEM output accumulator with P taken straight
+//              from tensor memory (A operand in TMEM), so the tensor core computes the next
+//              scores while the softmax warps work on this tile;
+//   warps 2-5  softmax: one query row per thread (TMEM lane = row); the row's scores are
+//              read into registers (which frees the score buffer at once) and its P goes
+//              back into one of two TMEM P buffers as bf16/fp16 pairs; the output is
+//              rescaled only when a row maximum grows by more than 2^8 (the final 1/l
 //              normalisation absorbs the stale maximum), then the epilogue.
-// TMEM: O in columns [0, D), score buffers at D and D + BN (512 columns allocated).
+// TMEM (512 columns): O in [0, D), NSB score buffers of BN columns, two P buffers of BN/2
+// columns.  P never touches shared memory: no P stores, no P operand reads.
 // Every wait is bounded; a wait that gives up sets the device error word and the CTA
 // drains its copies, frees TMEM and exits.
 #include "flash_prefill.cuh"
@@ -36,26 +39,26 @@ constexpr int fa_tc_bn(int) { return 128; }
 template <int D>
 struct FaTc {
   static constexpr int BM = 128;
-  // what fits in 227 KB next to Q: at D = 256 one K/V stage and one P buffer
+  // what fits in 227 KB next to Q: at D = 256 one K/V stage
   static constexpr int BN = fa_tc_bn(D);
-  static constexpr int NS = D == 256 ? 1 : D == 128 ? 2 : 3;  // K/V ring stages
-  static constexpr int NP = D == 256 ? 1 : 2;  // P buffers
+  static constexpr int NS = D == 256 ? 1 : D == 128 ? 3 : 4;  // K/V ring stages
+  static constexpr int NSB = D == 256 ? 1 : 2;                // TMEM score buffers
   static constexpr int DB = D / 64;
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KV_BYTES = BN * D * 2;
-  static constexpr uint32_t P_BYTES = BM * BN * 2;
   static constexpr uint32_t OFF_K = Q_BYTES;
   static constexpr uint32_t OFF_V = OFF_K + NS * KV_BYTES;
-  static constexpr uint32_t OFF_P = OFF_V + NS * KV_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_P + NP * P_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_V + NS * KV_BYTES;
   static constexpr uint32_t SMEM = OFF_BAR + 256 + 1024;
+  // TMEM columns: O, the score buffers, the two P buffers
+  static constexpr uint32_t COL_S = D, COL_P = D + NSB * BN;
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(D + 2 * BN <= 512, "TMEM budget");
+  static_assert(COL_P + 2 * (BN / 2) <= 512, "TMEM budget");
 };
 
 struct FaBars {
   uint64_t q_full;
-  uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
+  uint64_t k_full[4], k_empty[4], v_full[4], v_empty[4];
   uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
   uint64_t o_done;
   uint32_t tmem_base;
@@ -88,7 +91,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t phase) {
 template <typename T, int D, bool PAGED>
 __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constant__ FaTcParams p) {
   using C = FaTc<D>;
-  constexpr int BM = C::BM, BN = C::BN, NS = C::NS, NP = C::NP, DB = C::DB;
+  constexpr int BM = C::BM, BN = C::BN, NS = C::NS, NSB = C::NSB, DB = C::DB;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = align1024(smem_raw);
@@ -191,14 +194,14 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       auto issue_pv = [&](int i) -> bool {
         const int s = i % NS;
         if (!mbar_wait(&bars->v_full[s], (i / NS) & 1)) return false;
-        if (!mbar_wait(&bars->p_full[i % NP], (i / NP) & 1)) return false;
+        if (!mbar_wait(&bars->p_full[i & 1], (i >> 1) & 1)) return false;
         fence_after();
-        const uint32_t pa = smem_u32(smem + C::OFF_P + (i % NP) * C::P_BYTES);
+        const uint32_t pa = tmem + C::COL_P + (i & 1) * (BN / 2);  // P_i: lane = row, 2 keys per column
         const uint32_t va = smem_u32(smem + C::OFF_V + s * C::KV_BYTES);
 #pragma unroll
         for (int ks = 0; ks < BN / 16; ++ks)
-          mma_f16(tmem, desc_kmajor(pa, BM, ks), desc_mnmajor(va, BN * 128, ks), id_o, i > 0 || ks > 0);
-        commit(&bars->p_free[i % NP]);
+          mma_f16_ts(tmem, pa + ks * 8, desc_mnmajor(va, BN * 128, ks), id_o, i > 0 || ks > 0);
+        commit(&bars->p_free[i & 1]);
         commit(&bars->v_empty[s]);
         return true;
       };
@@ -206,14 +209,14 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int s = j % NS;
         ok = mbar_wait(&bars->k_full[s], (j / NS) & 1);
-        if (ok && j >= 2) ok = mbar_wait(&bars->s_free[j & 1], ((j - 2) >> 1) & 1);
+        if (ok && j >= NSB) ok = mbar_wait(&bars->s_free[j % NSB], ((j - NSB) / NSB) & 1);
         if (!ok) break;
         fence_after();
         const uint32_t ka = smem_u32(smem + C::OFF_K + s * C::KV_BYTES);
-        const uint32_t sc = tmem + D + (j & 1) * BN;
+        const uint32_t sc = tmem + C::COL_S + (j % NSB) * BN;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) mma_f16(sc, desc_kmajor(qa, BM, ks), desc_kmajor(ka, BN, ks), id_s, ks > 0);
-        commit(&bars->s_full[j & 1]);
+        commit(&bars->s_full[j % NSB]);
         commit(&bars->k_empty[s]);
         if (j >= 1) ok = issue_pv(j - 1);
       }
@@ -232,15 +235,15 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      if (!(ok = warp_wait(&bars->s_full[j & 1], (j >> 1) & 1))) break;
+      if (!(ok = warp_wait(&bars->s_full[j % NSB], (j / NSB) & 1))) break;
       fence_after();
       float x[BN];
 #pragma unroll
-      for (int c = 0; c < BN; c += 16) tmem_ld16(lt + D + (j & 1) * BN + c, x + c);
+      for (int c = 0; c < BN; c += 16) tmem_ld16(lt + C::COL_S + (j % NSB) * BN + c, x + c);
       tmem_wait_ld();
       fence_before();
       __syncwarp();
-      if (lane == 0) tma::arrive(&bars->s_free[j & 1]);
+      if (lane == 0) tma::arrive(&bars->s_free[j % NSB]);
 
       const int j0 = j * BN;
       const bool need_mask = (j0 + BN > kv_len) || (p.causal && j0 + BN - 1 > qoff + q0);
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       const bool grow = m_new > m + 8.f;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // rescale this warp's output rows once PV_{j-1} has landed
-        if (!(ok = warp_wait(&bars->p_free[(j - 1) % NP], ((j - 1) / NP) & 1))) break;
+        if (!(ok = warp_wait(&bars->p_free[(j - 1) & 1], ((j - 1) >> 1) & 1))) break;
         fence_after();
         const float f = grow ? ex2(m - m_new) : 1.f;
 #pragma unroll 1
@@ -277,25 +280,35 @@ __global__ void __launch_bounds__(kThreads, 1) fa_tc_kernel(const __grid_constan
       }
       if (grow) m = m_new;
       const float nbase = m == -INFINITY ? 0.f : -m;
-      if (j >= NP && !(ok = warp_wait(&bars->p_free[j % NP], ((j - NP) / NP) & 1))) break;
-      char* pb = smem + C::OFF_P + (j % NP) * C::P_BYTES;
+      // P_j into TMEM P buffer j & 1, once PV_{j-2} has read it
+      if (j >= 2 && !(ok = warp_wait(&bars->p_free[j & 1], ((j - 2) >> 1) & 1))) break;
+      const uint32_t pt = lt + C::COL_P + (j & 1) * (BN / 2);
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c8 = 0; c8 < BN / 8; ++c8) {
-        float e[8];
+      for (int c32 = 0; c32 < BN / 32; ++c32) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          e[i] = ex2(fmaf(x[c8 * 8 + i], p.scale_log2, nbase));
-          rs4[i & 3] += e[i];
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float e[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            e[i] = ex2(fmaf(x[c32 * 32 + c8 * 8 + i], p.scale_log2, nbase));
+            rs4[i & 3] += e[i];
+          }
+          const uint4 u = pack8<T>(e);  // element 2t in the low half of word t
+          pk[c8 * 4] = u.x;
+          pk[c8 * 4 + 1] = u.y;
+          pk[c8 * 4 + 2] = u.z;
+          pk[c8 * 4 + 3] = u.w;
         }
-        *reinterpret_cast<uint4*>(pb + (c8 >> 3) * (BM * 128) + sw128(r, c8 & 7)) = pack8<T>(e);
+        tmem_st16(pt + c32 * 16, reinterpret_cast<const float*>(pk));
       }
       const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l += rs;
-      fence_async_smem();
+      tmem_wait_st();
       fence_before();
       __syncwarp();
-      if (lane == 0) tma::arrive(&bars->p_full[j % NP]);
+      if (lane == 0) tma::arrive(&bars->p_full[j & 1]);
     }
     if (ok && n_tiles > 0) ok = warp_wait(&bars->o_done, 0);
     if (ok) {

@@ -75,6 +75,18 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1 : 0));
 }
 
+// A operand in tensor memory: lane m holds row m of A, K-major, two 16-bit elements per
+// 32-bit column (the even K index in the low half); k-step ks of a K = 16 MMA starts at
+// column a_tmem + 8 ks.  The instruction descriptor must say K-major for A.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1 : 0));
+}
+
 // Arrive on `mbar` once every MMA this thread issued so far has completed.
 __device__ __forceinline__ void commit(uint64_t* mbar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
