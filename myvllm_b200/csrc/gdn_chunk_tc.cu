@@ -9,8 +9,8 @@
 //
 // Per chunk (^T on a per-chunk 64-token axis; every contraction has the 128-wide feature
 // dimension as the MMA M):
-//   D1   = [q; k] k^T on the raw inputs          (M = 64 q rows + 64 k rows, N = 64, K = 128)
-//          with the q/k L2 norms applied to the fp32 products:
+//   D1   = [q; k] [q; k]^T on the raw inputs    (M = N = 64 q rows + 64 k rows, K = 128);
+//          its diagonal gives the q/k L2 norms, which are applied to the fp32 products:
 //          Aqk = lower(scale D1[q] e^{G_i-G_j} / |q_i||k_j|),
 //          A   = strict_lower(beta_i D1[k] e^{G_i-G_j} / |k_i||k_j|)
 //   Ti   = (I + A)^-1                           (blocked, fp32-accurate: see solve_tril64)
@@ -53,7 +53,7 @@ constexpr int kPrep = 256, kRec = 128, kThreads = kPrep + kRec;
 constexpr int kBarPrep = 1, kBarRec = 2;  // named barriers
 constexpr int kMaxSort = 512;
 
-// TMEM columns
+// TMEM columns (D1 is the 128 x 128 Gram matrix [q; k][q; k]^T: q columns, then k columns)
 constexpr uint32_t COL_S = 0, COL_O = 128, COL_U = 192 /* two 64-column buffers */, COL_W = 320, COL_D1 = 384;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
   umma::fence_after();
   const uint32_t tmem = tmem_slot;
   const int n_chains = S * p.hv;
-  const uint32_t id_d1 = umma::idesc_f16(128, 64, false, false, false, kBf16);
+  const uint32_t id_d1 = umma::idesc_f16(128, 128, false, false, false, kBf16);
 
   if (tid < kPrep) {
     // =============================================================== prep group
@@ -637,37 +637,16 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       bool w = umma::mbar_wait(&bars.raw_qk[kk & 1], (kk >> 1) & 1);
       if (tid == 0) qk_used = kk + 1;
       if (!(w = bar_and(kBarPrep, kPrep, w))) return false;
-      const char* qk = sm + SM_QK + (kk & 1) * 32768;
       if (tid == 0) {
+        // D1 = [q; k] [q; k]^T: one 128-row K-major operand as both A and B
         umma::fence_after();
-        const uint32_t qk_a = smem_u32(qk);
+        const uint32_t qk_a = smem_u32(sm + SM_QK + (kk & 1) * 32768);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t koff = (ks >> 2) * 16384 + (ks & 3) * 32;
-          umma::mma_f16(tmem + COL_D1, umma::smem_desc(qk_a + koff, 16, 1024),
-                        umma::smem_desc(qk_a + 8192 + koff, 16, 1024), id_d1, ks > 0);
+          const uint64_t d = umma::smem_desc(qk_a + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+          umma::mma_f16(tmem + COL_D1, d, d, id_d1, ks > 0);
         }
         umma::commit(&bars.d1_done);
-      }
-      float* fs = sF + (kk & 1) * kFSet;
-      const int row = tid >> 1, hh = tid & 1;  // rows 0-63 q, 64-127 k
-      float ss = 0.f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float f[8];
-        unpack8<T>(*reinterpret_cast<const uint4*>(qk + hh * 16384 + umma::sw128(row, c)), f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
-      }
-      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-      const float nf = p.l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
-      if (hh == 0) {
-        if (row < 64) {
-          fs[F_QN + row] = nf;
-        } else {
-          fs[F_KN + row - 64] = nf;
-          fs[F_GC + row - 64] = p.l2norm ? fs[F_G + row - 64] + 0.5f * log2f(ss + 1e-6f) : fs[F_G + row - 64];
-        }
       }
       return true;
     };
@@ -676,6 +655,28 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       bool w = umma::mbar_wait(&bars.d1_done, kk & 1);
       if (!(w = bar_and(kBarPrep, kPrep, w))) return false;
       umma::fence_after();
+      // q/k norms from the Gram diagonal, D1[r][r] = |row r|^2 (rows 0-63 q, 64-127 k):
+      // warps 0-3, thread = TMEM lane = row, picking column r of its warp's 32 columns
+      if (tid < 128) {
+        float v[32];
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + lane_base), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + lane_base + 16), v + 16);
+        umma::tmem_wait_ld();
+        float ss = v[0];
+#pragma unroll
+        for (int j = 1; j < 32; ++j) ss = lane == j ? v[j] : ss;
+        float* fs = sF + (kk & 1) * kFSet;
+        const int row = tid;
+        const float nf = p.l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
+        if (row < 64) {
+          fs[F_QN + row] = nf;
+        } else {
+          fs[F_KN + row - 64] = nf;
+          fs[F_GC + row - 64] = p.l2norm ? fs[F_G + row - 64] + 0.5f * log2f(ss + 1e-6f) : fs[F_G + row - 64];
+        }
+      }
+      umma::fence_before();
+      bar_sync(kBarPrep, kPrep);
       if (tid == 0) {
         Rec r;
         r.seq = it.seq;
@@ -725,8 +726,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       // masked entries may overflow before the select drops them.
       if (tl >= 64) {
         float v[32];
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + 64 + wg * 32), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + 64 + wg * 32 + 16), v + 16);
         const int i = tl - 64;
         const float rowf = sFk[F_B + i] * sFk[F_KN + i];
         const float gi = sFk[F_G + i];
@@ -807,8 +808,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       }
       if (tl < 64) {
         float v[32];
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32), v);
-        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + wg * 32 + 16), v + 16);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + 64 + wg * 32), v);
+        umma::tmem_ld16(umma::taddr(tmem, lane_base, COL_D1 + 64 + wg * 32 + 16), v + 16);
         const int i = tl;
         const float rowf = p.scale * sFk[F_QN + i];
         const float gi = sFk[F_G + i];
@@ -891,7 +892,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
     // applies it to the op's output.
     auto store_o = [&]() {
       if constexpr (!NORM) {
-        for (int e = rt; e < C * 16; e += kRec) {
+        // warps 9-11 only: warp 8's lane 0 issues the U/W products meanwhile
+        for (int e = rt - 32; e < C * 16; e += kRec - 32) {
+          if (e < 0) break;
           const int i = e >> 4, c16 = e & 15;
           if (i < pend_n) {
             const uint4 val = *reinterpret_cast<const uint4*>(sm + SM_O + (c16 >> 3) * 8192 + umma::sw128(i, c16 & 7));
