@@ -1256,12 +1256,20 @@ int launch_chunk_tc(const mvb_tensor* q, const mvb_tensor* k, const mvb_tensor* 
     cfg.numAttrs = p.balanced ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, p);
   };
-  cudaError_t e;
-  if (q->dtype == MVB_BF16)
-    e = norm ? go(gdn_chunk_tc_kernel<__nv_bfloat16, true>, mask_bf_norm)
-             : go(gdn_chunk_tc_kernel<__nv_bfloat16, false>, mask_bf);
-  else
-    e = norm ? go(gdn_chunk_tc_kernel<__half, true>, mask_h_norm) : go(gdn_chunk_tc_kernel<__half, false>, mask_h);
+  auto launch = [&]() -> cudaError_t {
+    if (q->dtype == MVB_BF16)
+      return norm ? go(gdn_chunk_tc_kernel<__nv_bfloat16, true>, mask_bf_norm)
+                  : go(gdn_chunk_tc_kernel<__nv_bfloat16, false>, mask_bf);
+    return norm ? go(gdn_chunk_tc_kernel<__half, true>, mask_h_norm) : go(gdn_chunk_tc_kernel<__half, false>, mask_h);
+  };
+  cudaError_t e = launch();
+  if (e == cudaErrorCooperativeLaunchTooLarge && p.balanced) {
+    // fewer SMs usable than the grid (e.g. an MPS thread limit): whole chains through the
+    // dynamic counter need no co-residency (work[0] and work[1] are the same words)
+    (void)cudaGetLastError();
+    p.balanced = 0;
+    e = launch();
+  }
   if (e != cudaSuccess) MVB_FAIL(MVB_ERR_CUDA, "chunk_gated_delta_rule: launch failed: %s", cudaGetErrorString(e));
   MVB_CHECK_LAUNCH("chunk_gated_delta_rule");
   return MVB_OK;
