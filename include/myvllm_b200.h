@@ -100,10 +100,12 @@ int mvb_causal_conv1d_update(const mvb_tensor* x, const mvb_tensor* weight, mvb_
  * workspace: NULL, or zero-initialised device memory that the kernel keeps ready for the
  * next launch:
  *   >= mvb_chunk_gated_delta_rule_workspace_size() bytes: the (sequence, v-head) chains are
- *      balanced over the SMs.  Laid end to end, they are cut into one equal span per SM;
- *      a chain cut at a span boundary runs its first part on one SM and its rest on the
- *      next, the state passing through recurrent_state under a flag in the workspace
- *      (cooperative launch; results are bit-identical to whole-chain scheduling);
+ *      balanced over the SMs.  Laid end to end, they are cut into one equal span per pair
+ *      of SMs (which run the two v-heads of a k-head side by side); a chain cut at a span
+ *      boundary runs its first part on one SM and its rest on the next pair, the state
+ *      passing through recurrent_state under a flag in the workspace (cooperative launch,
+ *      or whole chains through the counter when the driver refuses one; results are
+ *      bit-identical to whole-chain scheduling);
  *   8 bytes up to that: a work counter, whole chains scheduled dynamically, longest first;
  *   NULL: whole chains round-robin.
  * Launches that share one workspace must be ordered (same stream). */

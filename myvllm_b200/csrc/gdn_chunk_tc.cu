@@ -439,17 +439,18 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_chunk_tc_kernel(const __grid_
       }
     };
     // Balanced schedule (McNaughton's wrap-around rule, with the order of the two cut
-    // parts chosen for a serial chain): the chains laid end to end in schedule order
-    // (sequences longest first, heads in order) cover ntot chunks; CTA i owns positions
-    // [i cs, (i+1) cs), cs = max(ceil(ntot / grid), longest chain), so the makespan is
-    // about ntot / grid chunks instead of what whole chains allow.  A chain cut at the
-    // span's end (the tail cut) runs FIRST and stores its state for the next CTA; a chain
-    // cut at the span's start (the head cut) runs LAST and first waits for the previous
-    // CTA's hand-off.  The two parts of a chain together are at most cs long, so the first
-    // part is normally done before the second is reached.  Thread 0 only.
-    // CTA pairs (2m, 2m + 1) run the two v-heads of one unit -- (sequence, v-heads 2j and
-    // 2j + 1), which share a k-head -- side by side, cut at the same places: the two SMs of
-    // a TPC then work on the same q/k tiles and the same code in step
+    // parts chosen for a serial chain).  A unit is one sequence's v-heads 2j and 2j + 1,
+    // which share a k-head; the CTA pair (2m, 2m + 1) runs its two chains side by side, cut
+    // at the same places, so the two SMs of a TPC work on the same q/k tiles and the same
+    // code in step (unpaired when Hv or the grid is odd).  The units laid end to end in
+    // schedule order (sequences longest first) cover ntot chunks; pair m owns positions
+    // [m cs, (m+1) cs), cs = max(ceil(ntot / pairs), longest chain), so the makespan is
+    // about ntot / pairs chunks instead of what whole chains allow.  A unit cut at the
+    // span's end (the tail cut) runs FIRST and stores its states for the next pair; a unit
+    // cut at the span's start (the head cut) runs LAST and first waits for the hand-off of
+    // the previous pair's CTA on the same lane.  The two parts of a unit together are at
+    // most cs long, so the first is normally done before the second is reached.  Thread 0
+    // only.
     const int pair = (p.hv % 2 == 0 && gridDim.x % 2 == 0) ? 2 : 1;
     const int hu = p.hv / pair, ulane = (int)blockIdx.x % pair;  // units per sequence; v-head in the unit
     int ph = 3, br = 0, bh = 0;           // phase; next whole unit (rank, unit head)
